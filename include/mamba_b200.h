@@ -1,0 +1,265 @@
+/*
+ * mamba_b200.h -- C ABI of the B200 (sm_100a) Mamba-1 selective-scan and causal-conv1d library
+ * (libmamba_b200.so).
+ *
+ * This is the drop-in boundary below the Python ops. It replaces the reference's nanobind module
+ * `mamba_cpu._C` (SandyTheAdventurer/mamba-cpu, csrc/bindings.cpp) and the torch-CPU conv path:
+ * plain pointers and sizes, no torch types, an int status instead of exceptions, and a CUDA stream
+ * argument where the reference takes a thread count (`num_threads`, bindings.cpp:35,60).
+ *
+ * Conventions for every entry point:
+ *  - Pointers are DEVICE pointers unless stated. NULL means an absent optional input, exactly as
+ *    the reference's 0-for-None uintptr convention (bindings.cpp:10-15, selective_scan.h:20).
+ *  - The caller allocates every output (selective_scan_interface.py:33-34, 72-79). Entry points
+ *    that need scratch take a caller-provided workspace whose size is returned by the matching
+ *    *_workspace_size function; they never allocate, except the *_f32 mirrors (below), which keep
+ *    the reference's signature and therefore allocate their scratch stream-ordered
+ *    (cudaMallocAsync / cudaFreeAsync on the given stream) as the reference allocates its own
+ *    (selective_scan.cpp:322, 341-342).
+ *  - Work is enqueued on `stream` (a cudaStream_t; NULL = the legacy default stream) and the call
+ *    returns without synchronising. Argument errors are detected before anything is enqueued.
+ *  - Kernels never trap: a bad argument is an error status, never a device fault.
+ */
+#ifndef MAMBA_B200_H
+#define MAMBA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define MB200_API __attribute__((visibility("default")))
+#else
+#define MB200_API
+#endif
+
+/* ---- status codes ------------------------------------------------------------------------ */
+#define MB200_OK 0
+#define MB200_ERR_NULL_POINTER 1 /* a required pointer is NULL */
+#define MB200_ERR_BAD_SHAPE 2    /* negative size, dim % ngroups != 0, ... */
+#define MB200_ERR_BAD_DTYPE 3    /* unknown or unsupported dtype code / combination */
+#define MB200_ERR_BAD_LAYOUT 4   /* stride or alignment outside what the kernel accepts */
+#define MB200_ERR_UNSUPPORTED 5  /* a valid request outside this build (e.g. dstate > 16) */
+#define MB200_ERR_WORKSPACE 6    /* workspace NULL or smaller than *_workspace_size */
+#define MB200_ERR_CUDA 7         /* a CUDA runtime call failed (launch error, allocation) */
+
+/* ---- dtype codes ------------------------------------------------------------------------- */
+#define MB200_F32 0
+#define MB200_BF16 1
+#define MB200_F16 2
+
+/* Largest dstate the scan kernels accept (Mamba-1 uses 16). */
+#define MB200_MAX_DSTATE 16
+/* Timesteps between the states the forward saves for the backward (chunk_states). */
+#define MB200_CHUNK 64
+
+/* ---- selective scan ---------------------------------------------------------------------- */
+
+/*
+ * Forward scan parameters. Shapes (elements; all dense unless a stride is given):
+ *   u, delta, z, out : (batch, dim, seqlen), dtype io_dtype, contiguous
+ *   A                : (dim, dstate) float32, contiguous
+ *   B, C             : (batch, ngroups, dstate, seqlen), dtype bc_dtype, element strides given
+ *                      below. seqlen stride 1 (the upstream layout) takes the vectorised path;
+ *                      any other stride -- e.g. dstate (the reference kernel's (b, g, l, n)
+ *                      layout, selective_scan.h:17) -- is accepted on a scalar-load path.
+ *   D, delta_bias    : (dim) float32 or NULL
+ *   last_state       : (batch, dim, dstate) float32 or NULL
+ *   chunk_states     : (batch, dim, ceil(seqlen / MB200_CHUNK), dstate) float32 or NULL: the state
+ *                      after every MB200_CHUNK timesteps, which the backward uses instead of
+ *                      recomputing the forward from t = 0.
+ * io_dtype in {F32, BF16, F16}; bc_dtype is F32 or equal to io_dtype.
+ */
+typedef struct mb200_scan_fwd_params {
+  const void* u;
+  const void* delta;
+  const float* A;
+  const void* B;
+  const void* C;
+  const float* D;
+  const void* z;
+  const float* delta_bias;
+  void* out;
+  float* last_state;
+  float* chunk_states;
+  int64_t batch, dim, seqlen, dstate, ngroups;
+  int64_t B_batch_stride, B_group_stride, B_dstate_stride, B_seqlen_stride;
+  int64_t C_batch_stride, C_group_stride, C_dstate_stride, C_seqlen_stride;
+  int32_t io_dtype;
+  int32_t bc_dtype;
+  int32_t delta_softplus;
+  int32_t reserved;
+} mb200_scan_fwd_params;
+
+/*
+ * Backward scan parameters: the forward inputs (`fwd`; its out/last_state are ignored, its
+ * chunk_states -- if not NULL -- must hold what the forward wrote) plus
+ *   dout             : (batch, dim, seqlen) io_dtype
+ *   dlast_state      : (batch, dim, dstate) float32 or NULL
+ * and outputs
+ *   du, ddelta       : (batch, dim, seqlen) io_dtype
+ *   dz               : (batch, dim, seqlen) io_dtype; required iff fwd.z != NULL
+ *   dA               : (dim, dstate) float32, summed over batch
+ *   dB, dC           : (batch, ngroups, dstate, seqlen) contiguous, dtype dbc_dtype (F32 or
+ *                      fwd.bc_dtype); overwritten
+ *   dD, ddelta_bias  : (dim) float32, summed over batch; either may be NULL to skip it
+ * The reference returns dA/dD/ddelta_bias as per-batch partials that its Python layer sums
+ * (selective_scan_interface.py:87); here the sum over batch happens on the device.
+ */
+typedef struct mb200_scan_bwd_params {
+  mb200_scan_fwd_params fwd;
+  const void* dout;
+  const float* dlast_state;
+  void* du;
+  void* ddelta;
+  void* dz;
+  float* dA;
+  void* dB;
+  void* dC;
+  float* dD;
+  float* ddelta_bias;
+  int32_t dbc_dtype;
+  int32_t reserved;
+} mb200_scan_bwd_params;
+
+/* Forward selective scan.
+ * Replaces mamba_cpu::selective_scan_fwd_f32 (csrc/selective_scan.h:40, bound at
+ * csrc/bindings.cpp:23-45) behind the op mamba_cpu::selective_scan_fwd
+ * (src/mamba_cpu/ops/selective_scan_interface.py:16-40). */
+MB200_API int mb200_selective_scan_fwd(const mb200_scan_fwd_params* p, void* stream);
+
+/* Bytes of device workspace mb200_selective_scan_bwd needs for these parameters (0 on bad
+ * arguments). Depends on shapes and on whether fwd.chunk_states is NULL, not on pointer values. */
+MB200_API size_t mb200_selective_scan_bwd_workspace_size(const mb200_scan_bwd_params* p);
+
+/* Backward selective scan. `workspace` must be 256-byte aligned and hold at least
+ * mb200_selective_scan_bwd_workspace_size(p) bytes; it need not be initialised.
+ * Replaces mamba_cpu::selective_scan_bwd_f32 (csrc/selective_scan.h:65, bound at
+ * csrc/bindings.cpp:47-84) behind mamba_cpu::selective_scan_bwd
+ * (src/mamba_cpu/ops/selective_scan_interface.py:48-87). */
+MB200_API int mb200_selective_scan_bwd(const mb200_scan_bwd_params* p, void* workspace,
+                                       size_t workspace_bytes, void* stream);
+
+/* Exact mirror of the reference binding `selective_scan_fwd_f32` (csrc/bindings.cpp:23-45):
+ * same argument order and meaning -- float32 everywhere, B/C in the reference kernel's
+ * (batch, ngroups, seqlen, dstate) layout (selective_scan.h:17) -- with `stream` in place of
+ * num_threads. last_state may be NULL. */
+MB200_API int mb200_selective_scan_fwd_f32(const float* u, const float* delta, const float* A,
+                                           const float* B, const float* C, const float* D,
+                                           const float* z, const float* delta_bias, float* out,
+                                           float* last_state, int64_t batch, int64_t dim,
+                                           int64_t seqlen, int64_t dstate, int64_t ngroups,
+                                           int delta_softplus, void* stream);
+
+/* Exact mirror of the reference binding `selective_scan_bwd_f32` (csrc/bindings.cpp:47-84),
+ * float32, B/C/dB/dC in (batch, ngroups, seqlen, dstate). As in the reference, dA_part (batch,
+ * dim, dstate), dD_part (batch, dim) and ddelta_bias_part (batch, dim) are per-batch partials.
+ * dB/dC are overwritten (the reference accumulates into zero-initialised buffers,
+ * selective_scan.h:47, which gives the same result). Scratch is allocated stream-ordered. */
+MB200_API int mb200_selective_scan_bwd_f32(
+    const float* u, const float* delta, const float* A, const float* B, const float* C,
+    const float* D, const float* z, const float* delta_bias, const float* dout,
+    const float* dlast_state, float* du, float* ddelta, float* dA_part, float* dB, float* dC,
+    float* dD_part, float* dz, float* ddelta_bias_part, int64_t batch, int64_t dim,
+    int64_t seqlen, int64_t dstate, int64_t ngroups, int delta_softplus, void* stream);
+
+/* ---- causal depthwise conv1d ------------------------------------------------------------- */
+
+/*
+ *   x, out        : (batch, dim, seqlen), dtype x_dtype (F32 / BF16 / F16), contiguous
+ *   weight        : (dim, width) float32, 1 <= width <= 8
+ *   bias          : (dim) float32 or NULL
+ *   initial_states: (batch, dim, width - 1) x_dtype or NULL (zeros)
+ *   final_states  : (batch, dim, width - 1) x_dtype or NULL: the last width-1 inputs of
+ *                   [initial_states | x] (causal_conv1d.py:48-53)
+ *   activation    : 0 = none, 1 = SiLU
+ */
+typedef struct mb200_conv1d_params {
+  const void* x;
+  const float* weight;
+  const float* bias;
+  const void* initial_states;
+  void* out;
+  void* final_states;
+  int64_t batch, dim, seqlen, width;
+  int32_t x_dtype;
+  int32_t activation;
+} mb200_conv1d_params;
+
+/* Causal depthwise conv1d with optional SiLU. Replaces the F.conv1d path of
+ * causal_conv1d_fn (src/mamba_cpu/ops/causal_conv1d.py:16-53). */
+MB200_API int mb200_causal_conv1d_fwd(const mb200_conv1d_params* p, void* stream);
+
+/* Backward of mb200_causal_conv1d_fwd (torch autograd's gradient of causal_conv1d.py:37-47):
+ *   dout (batch, dim, seqlen) x_dtype -> dx (x_dtype), dweight (dim, width) f32,
+ *   dbias (dim) f32 or NULL, dinitial_states (batch, dim, width-1) x_dtype or NULL. */
+MB200_API size_t mb200_causal_conv1d_bwd_workspace_size(const mb200_conv1d_params* p);
+MB200_API int mb200_causal_conv1d_bwd(const mb200_conv1d_params* p, const void* dout, void* dx,
+                                      float* dweight, float* dbias, void* dinitial_states,
+                                      void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- decode steps (the reference runs these in plain PyTorch) --------------------------- */
+
+/*
+ * One selective-scan step per (batch, channel) updating `state` in place.
+ * Replaces selective_state_update (src/mamba_cpu/ops/selective_state_update.py:5-57) for the
+ * Mamba-1 layout; the multi-head layout is the same after flattening (heads*headdim -> dim):
+ *   state (batch, dim, dstate) float32 or io_dtype (state_dtype); x, dt, z, out (batch, dim)
+ *   io_dtype; A (dim, dstate) f32; B, C (batch, ngroups, dstate) bc_dtype contiguous;
+ *   D, dt_bias (dim) f32 or NULL.
+ */
+typedef struct mb200_state_update_params {
+  void* state;
+  const void* x;
+  const void* dt;
+  const float* A;
+  const void* B;
+  const void* C;
+  const float* D;
+  const void* z;
+  const float* dt_bias;
+  void* out;
+  int64_t batch, dim, dstate, ngroups;
+  int32_t io_dtype, bc_dtype, state_dtype;
+  int32_t dt_softplus;
+} mb200_state_update_params;
+
+MB200_API int mb200_selective_state_update(const mb200_state_update_params* p, void* stream);
+
+/*
+ * Decode conv step(s): causal_conv1d_update (src/mamba_cpu/ops/causal_conv1d.py:56-85).
+ *   x, out (batch, dim, seqlen) x_dtype; conv_state (batch, dim, state_len) x_dtype, rolled in
+ *   place by seqlen steps; state_len >= width - 1; weight (dim, width) f32; bias f32 or NULL.
+ */
+typedef struct mb200_conv1d_update_params {
+  const void* x;
+  void* conv_state;
+  const float* weight;
+  const float* bias;
+  void* out;
+  int64_t batch, dim, seqlen, state_len, width;
+  int32_t x_dtype;
+  int32_t activation;
+} mb200_conv1d_update_params;
+
+MB200_API int mb200_causal_conv1d_update(const mb200_conv1d_update_params* p, void* stream);
+
+/* ---- misc -------------------------------------------------------------------------------- */
+
+/* Static description of a status code. */
+MB200_API const char* mb200_status_string(int status);
+
+/* Library ABI version: (major << 16) | minor. */
+MB200_API int mb200_version(void);
+
+/* Number of kernel launches the most recent successful call on this host thread enqueued. */
+MB200_API int mb200_last_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MAMBA_B200_H */

@@ -1,0 +1,68 @@
+// scan.cuh -- kernel-side argument blocks and launcher declarations of the selective scan.
+#pragma once
+
+#include "common.cuh"
+
+namespace mb200 {
+
+// Warps per CTA of the forward / backward scan kernels.
+constexpr int kFwdWarps = 4;
+constexpr int kBwdWarps = 4;
+
+// Kernel-side view of one selective-scan call. Built and validated on the host from
+// mb200_scan_fwd_params / mb200_scan_bwd_params (capi.cu).
+struct ScanArgs {
+  const void* u;
+  const void* delta;
+  const float* A;
+  const void* B;
+  const void* C;
+  const float* D;
+  const void* z;
+  const float* delta_bias;
+  void* out;            // forward output (io dtype), NULL in the states-only pass
+  float* last_state;    // (batch, dim, dstate) or NULL
+  float* chunk_states;  // (batch, dim, nchunks, dstate) or NULL
+  int64_t batch, dim, L, N, ngroups, dpg;
+  int64_t sBb, sBg, sBn, sBl, sCb, sCg, sCn, sCl;
+  int tiles;    // CTAs per (batch, group) slice
+  int nchunks;  // ceil(L / kChunk)
+  int softplus;
+  int vec_io;   // u / delta / z / out rows allow 16-byte vector access
+  int vec_bc;   // B / C are l-contiguous and aligned
+};
+
+struct BwdArgs {
+  ScanArgs f;
+  const float* states;  // chunk_states of the forward (or of the states pass)
+  const void* dout;
+  const float* dlast;
+  void* du;
+  void* ddelta;
+  void* dz;
+  float* part_bc;   // (batch*ngroups, clusters, 2, N, Lpad) cluster partial sums of dB | dC
+  float* part_A;    // (batch, dim, N)
+  float* part_D;    // (batch, dim)
+  float* part_db;   // (batch, dim)
+  int64_t Lpad;     // nchunks * kChunk
+  int clusters;     // clusters per slice = tiles / cluster size
+};
+
+// Segments per channel (time-parallel lanes) the launchers pick for a call.
+int fwd_segments(int64_t rows);
+int bwd_segments(int64_t rows);
+int bwd_cluster_size(int64_t tiles);
+
+cudaError_t launch_scan_fwd(const ScanArgs& a, int io_dtype, int bc_dtype, bool write_out,
+                            cudaStream_t stream);
+cudaError_t launch_scan_bwd(const BwdArgs& a, int io_dtype, int bc_dtype, int cluster,
+                            cudaStream_t stream);
+// Sums the cluster partials of dB/dC over clusters (written with element strides osb/osg/osn/osl
+// for batch/group/state/seqlen) and dA/dD/ddelta_bias over batch (skipped with batch_partials,
+// when the kernel wrote the caller's per-batch partial buffers directly).
+cudaError_t launch_scan_bwd_reduce_strided(const BwdArgs& a, void* dB, void* dC, int dbc_dtype,
+                                           int64_t osb, int64_t osg, int64_t osn, int64_t osl,
+                                           float* dA, float* dD, float* db, bool batch_partials,
+                                           cudaStream_t stream);
+
+}  // namespace mb200

@@ -1,0 +1,25 @@
+"""B200-native (sm_100a) Mamba-1 selective scan and causal conv1d.
+
+The public functions have the signatures of mamba-cpu / mamba_ssm / causal_conv1d
+(mamba-cpu src/mamba_cpu/__init__.py:3-23) and run hand-written CUDA kernels from
+libmamba_b200.so on CUDA tensors. Non-CUDA tensors are rejected, as the reference rejects
+non-CPU ones.
+"""
+
+from mamba_cpu_b200 import parallel
+from mamba_cpu_b200.ops import (
+    causal_conv1d_fn,
+    causal_conv1d_update,
+    selective_scan_fn,
+    selective_state_update,
+)
+
+__version__ = "0.1.0"
+
+__all__ = [
+    "causal_conv1d_fn",
+    "causal_conv1d_update",
+    "parallel",
+    "selective_scan_fn",
+    "selective_state_update",
+]

@@ -1,0 +1,140 @@
+"""CUDA causal conv1d (+ SiLU), its backward and decode step vs the float64 oracle.
+
+Cases follow mamba-cpu tests/test_causal_conv1d.py (widths, activation, bias, state chaining,
+update == full conv, final_states_out, dtypes) and tests/test_upstream.py:107-130 (width 3)."""
+
+import numpy as np
+import pytest
+import torch
+
+import mamba_cpu_b200 as mb
+from helpers import assert_close, np64
+from oracle import f64
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("width", [1, 2, 3, 4, 8])
+@pytest.mark.parametrize("activation", [None, "silu"])
+@pytest.mark.parametrize("has_bias", [False, True])
+@pytest.mark.parametrize("shape", [(2, 8, 37), (2, 64, 100), (1, 16, 1), (3, 24, 2048 + 13)])
+def test_matches_oracle_fwd_bwd(width, activation, has_bias, shape):
+    torch.manual_seed(0)
+    x = torch.randn(*shape)
+    w = torch.randn(shape[1], width)
+    b = torch.randn(shape[1]) if has_bias else None
+    xg, wg = x.cuda().requires_grad_(), w.cuda().requires_grad_()
+    bg = b.cuda().requires_grad_() if b is not None else None
+    out = mb.causal_conv1d_fn(xg, wg, bg, activation=activation)
+    assert_close(out, f64.conv1d_fwd(x, w, b, None, activation), 1e-5, 1e-5, "out")
+    dout = torch.randn(*shape)
+    (out * dout.cuda()).sum().backward()
+    g = f64.conv1d_bwd(x, w, b, None, activation, dout)
+    assert_close(xg.grad, g["dx"], 1e-5, 1e-5, "dx")
+    sc = max(1.0, float(np.abs(g["dweight"]).max()))
+    assert_close(np64(wg.grad) / sc, g["dweight"] / sc, 1e-5, 1e-5, "dweight")
+    if b is not None:
+        sc = max(1.0, float(np.abs(g["dbias"]).max()))
+        assert_close(np64(bg.grad) / sc, g["dbias"] / sc, 1e-5, 1e-5, "dbias")
+
+
+def test_initial_and_final_states_chain():
+    torch.manual_seed(0)
+    x = torch.randn(2, 8, 40).cuda()
+    w = torch.randn(8, 4).cuda()
+    full = mb.causal_conv1d_fn(x, w, activation="silu")
+    a, state = mb.causal_conv1d_fn(x[..., :25], w, activation="silu", return_final_states=True)
+    b = mb.causal_conv1d_fn(x[..., 25:], w, initial_states=state, activation="silu")
+    torch.testing.assert_close(torch.cat([a, b], -1), full)
+
+
+@pytest.mark.parametrize("seqlen", [1, 2, 3, 40])
+def test_initial_states_gradients(seqlen):
+    torch.manual_seed(1)
+    x, w, bias, init = torch.randn(2, 8, seqlen), torch.randn(8, 4), torch.randn(8), torch.randn(2, 8, 3)
+    leaves = [t.cuda().requires_grad_() for t in (x, w, bias, init)]
+    out, fin = mb.causal_conv1d_fn(leaves[0], leaves[1], leaves[2], initial_states=leaves[3],
+                                   return_final_states=True, activation="silu")
+    o64, f64s = f64.conv1d_fwd(x, w, bias, init, "silu", return_final_states=True)
+    assert_close(out, o64, 1e-5, 1e-5, "out")
+    assert_close(fin, f64s, 0, 0, "final_states")
+    dout = torch.randn(2, 8, seqlen)
+    (out * dout.cuda()).sum().backward()
+    g = f64.conv1d_bwd(x, w, bias, init, "silu", dout)
+    for t, k in zip(leaves, ("dx", "dweight", "dbias", "dinitial_states")):
+        assert_close(t.grad, g[k], 1e-5, 1e-5, k)
+
+
+def test_final_states_gradient_flows():
+    torch.manual_seed(2)
+    x = torch.randn(1, 4, 2).cuda().requires_grad_()
+    init = torch.randn(1, 4, 3).cuda().requires_grad_()
+    w = torch.randn(4, 4).cuda()
+    _, fin = mb.causal_conv1d_fn(x, w, initial_states=init, return_final_states=True)
+    fin.sum().backward()
+    # final = [init | x][-3:] = init[..., 2:] ++ x
+    assert torch.equal(x.grad, torch.ones_like(x))
+    assert torch.equal(init.grad[..., 2:], torch.ones(1, 4, 1, device="cuda"))
+    assert not init.grad[..., :2].any()
+
+
+def test_final_states_out_buffer():
+    x = torch.randn(2, 8, 10).cuda()
+    w = torch.randn(8, 4).cuda()
+    buf = torch.empty(2, 8, 3, device="cuda")
+    _, final = mb.causal_conv1d_fn(x, w, return_final_states=True, final_states_out=buf)
+    assert final is buf
+    torch.testing.assert_close(buf, x[..., -3:])
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_low_precision_dtypes(dtype):
+    torch.manual_seed(0)
+    x = torch.randn(2, 64, 300).to(dtype)
+    w, b = torch.randn(64, 4), torch.randn(64)
+    out = mb.causal_conv1d_fn(x.cuda(), w.cuda(), b.cuda(), activation="silu")
+    assert out.dtype == dtype
+    assert_close(out, f64.conv1d_fwd(x, w, b, None, "silu"), 1e-2, 1e-2, "out")
+
+
+def test_rejects():
+    x, w = torch.randn(1, 4, 8).cuda(), torch.randn(4, 4).cuda()
+    with pytest.raises(NotImplementedError):
+        mb.causal_conv1d_fn(x, w, seq_idx=torch.zeros(1, 8, dtype=torch.int32, device="cuda"))
+    with pytest.raises(ValueError):
+        mb.causal_conv1d_fn(x, w, activation="relu")
+    with pytest.raises(ValueError):
+        mb.causal_conv1d_fn(x.cpu(), w.cpu())
+
+
+def test_update_matches_full_conv():
+    torch.manual_seed(0)
+    x = torch.randn(2, 8, 12).cuda()
+    w = torch.randn(8, 4).cuda()
+    bias = torch.randn(8).cuda()
+    full = mb.causal_conv1d_fn(x, w, bias, activation="silu")
+    state = torch.zeros(2, 8, 4, device="cuda")
+    steps = [mb.causal_conv1d_update(x[..., t], state, w, bias, "silu") for t in range(12)]
+    torch.testing.assert_close(torch.stack(steps, -1), full, rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("state_len", [3, 4, 6, 7])
+@pytest.mark.parametrize("seqlen", [1, 3, 5])
+def test_update_multi_token_matches_oracle(state_len, seqlen):
+    torch.manual_seed(0)
+    x = torch.randn(2, 64, seqlen)
+    w, bias = torch.randn(64, 4), torch.randn(64)
+    state = torch.randn(2, 64, state_len)
+    sg = state.cuda()
+    out = mb.causal_conv1d_update(x.cuda(), sg, w.cuda(), bias.cuda(), "silu")
+    o64, s64 = f64.conv1d_update(x, state, w, bias, "silu")
+    assert_close(out, o64, 1e-5, 1e-5, "out")
+    assert_close(sg, s64, 0, 0, "conv_state")
+
+
+def test_update_rejects():
+    x, st, w = torch.randn(1, 4).cuda(), torch.zeros(1, 4, 2).cuda(), torch.randn(4, 4).cuda()
+    with pytest.raises(ValueError):
+        mb.causal_conv1d_update(x, st, w)
+    with pytest.raises(NotImplementedError):
+        mb.causal_conv1d_update(x, torch.zeros(1, 4, 3).cuda(), w, cache_seqlens=torch.zeros(1).cuda())
