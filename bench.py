@@ -240,6 +240,15 @@ def run_ours(args):
     ms_step, ms_fwd, ms_bwd = stat.tolist()
 
     # ---- e2e through the public API: pinned H2D, fwd + autograd bwd, D2H of everything ----
+    if args.no_e2e:
+        del g_fwd, g_bwd
+        if group is not None:
+            dist.barrier()
+            dist.destroy_process_group()
+        if rank == 0:
+            print(json.dumps({"ms_fwd": ms_fwd, "ms_bwd": ms_bwd, "ms_per_step": ms_step,
+                              "value": E * world / (ms_step * 1e-3), "note": "--no-e2e run (profiling)"}))
+        return
     pinned = {k: (None if v is None else v.pin_memory()) for k, v in host.items()}
     outs_host = {}
     names_in = ["u", "delta", "A", "B", "C", "D", "z", "delta_bias"]
@@ -453,6 +462,7 @@ def main():
     p.add_argument("--config", default="c2", choices=sorted(CONFIGS))
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-e2e", action="store_true", help="kernel timing only (for profiler runs)")
     p.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of CPU baseline work")
     args = p.parse_args()
     if args.warmup < 3:

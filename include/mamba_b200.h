@@ -258,6 +258,11 @@ MB200_API int mb200_version(void);
 /* Number of kernel launches the most recent successful call on this host thread enqueued. */
 MB200_API int mb200_last_launch_count(void);
 
+/* Read and clear the device-side fault word of the current device (synchronises the device).
+ * Kernels never trap: a bounded wait that gave up (a staged copy that did not arrive in ~2.5 s)
+ * sets bit 0 and the kernel finishes with unspecified outputs. *fault = 0 means no fault. */
+MB200_API int mb200_device_fault(int* fault);
+
 #ifdef __cplusplus
 }
 #endif

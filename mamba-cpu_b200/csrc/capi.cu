@@ -299,14 +299,15 @@ MB200_API int mb200_selective_scan_bwd_f32(
 
 namespace {
 
-int build_conv_args(const mb200_conv1d_params* p, ConvArgs* a) {
+int build_conv_args(const mb200_conv1d_params* p, bool need_out, ConvArgs* a) {
   if (p == nullptr) return MB200_ERR_NULL_POINTER;
   if (p->batch < 0 || p->dim < 0 || p->seqlen < 0 || p->width < 1) return MB200_ERR_BAD_SHAPE;
   if (p->width > kConvMaxWidth) return MB200_ERR_UNSUPPORTED;
   if (!io_dtype_ok(p->x_dtype)) return MB200_ERR_BAD_DTYPE;
   if (p->activation != 0 && p->activation != 1) return MB200_ERR_BAD_SHAPE;
   const bool empty = p->batch == 0 || p->dim == 0;
-  if (!empty && (p->x == nullptr || p->weight == nullptr || p->out == nullptr)) return MB200_ERR_NULL_POINTER;
+  if (!empty && (p->x == nullptr || p->weight == nullptr || (need_out && p->out == nullptr)))
+    return MB200_ERR_NULL_POINTER;
   const int64_t span = (int64_t)kConvThreads * kConvItems;
   a->x = p->x;
   a->w = p->weight;
@@ -331,7 +332,7 @@ extern "C" {
 MB200_API int mb200_causal_conv1d_fwd(const mb200_conv1d_params* p, void* stream) {
   reset_launches();
   ConvArgs a;
-  int st = build_conv_args(p, &a);
+  int st = build_conv_args(p, true, &a);
   if (st != MB200_OK) return st;
   if (launch_conv_fwd(a, p->x_dtype, static_cast<cudaStream_t>(stream)) != cudaSuccess) return MB200_ERR_CUDA;
   if (a.batch > 0 && a.dim > 0) note_launches(1);
@@ -340,7 +341,7 @@ MB200_API int mb200_causal_conv1d_fwd(const mb200_conv1d_params* p, void* stream
 
 MB200_API size_t mb200_causal_conv1d_bwd_workspace_size(const mb200_conv1d_params* p) {
   ConvArgs a;
-  if (build_conv_args(p, &a) != MB200_OK) return 0;
+  if (build_conv_args(p, false, &a) != MB200_OK) return 0;
   return align_up(sizeof(float) * (size_t)conv_bwd_partials(a) * (size_t)(a.width + 1), 256);
 }
 
@@ -348,15 +349,14 @@ MB200_API int mb200_causal_conv1d_bwd(const mb200_conv1d_params* p, const void* 
                                       float* dweight, float* dbias, void* dinitial_states,
                                       void* workspace, size_t workspace_bytes, void* stream) {
   reset_launches();
+  if (p == nullptr) return MB200_ERR_NULL_POINTER;
   ConvArgs a;
-  mb200_conv1d_params q = *p;
-  if (q.out == nullptr) q.out = dx;  // the backward does not write `out`; only validate shapes
-  int st = build_conv_args(&q, &a);
+  int st = build_conv_args(p, false, &a);
   if (st != MB200_OK) return st;
   const bool empty = a.batch == 0 || a.dim == 0;
   if (!empty && (dout == nullptr || dx == nullptr)) return MB200_ERR_NULL_POINTER;
   if (a.dim > 0 && dweight == nullptr) return MB200_ERR_NULL_POINTER;
-  const size_t need = mb200_causal_conv1d_bwd_workspace_size(&q);
+  const size_t need = mb200_causal_conv1d_bwd_workspace_size(p);
   if (need > 0 && (workspace == nullptr || workspace_bytes < need ||
                    (reinterpret_cast<uintptr_t>(workspace) & 255) != 0))
     return MB200_ERR_WORKSPACE;
@@ -427,5 +427,13 @@ MB200_API const char* mb200_status_string(int status) {
 MB200_API int mb200_version(void) { return (1 << 16) | 0; }
 
 MB200_API int mb200_last_launch_count(void) { return g_launches; }
+
+MB200_API int mb200_device_fault(int* fault) {
+  if (fault == nullptr) return MB200_ERR_NULL_POINTER;
+  int f0 = 0, f1 = 0;
+  if (read_fault_fwd(&f0) != cudaSuccess || read_fault_bwd(&f1) != cudaSuccess) return MB200_ERR_CUDA;
+  *fault = f0 | f1;
+  return MB200_OK;
+}
 
 }  // extern "C"

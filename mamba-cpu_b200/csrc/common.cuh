@@ -11,8 +11,19 @@
 namespace mb200 {
 
 constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
 constexpr int kChunk = MB200_CHUNK;      // timesteps per chunk (chunk_states granularity)
 constexpr int kMaxState = MB200_MAX_DSTATE;
+
+// Staged B/C tile rows in shared memory: kChunk elements per row, stored as two halves. For 4-byte
+// elements the second half starts 16 bytes later than contiguous, so the 8 time-segment lanes of
+// a channel (each reading 16-byte pieces 32 bytes apart) fall in distinct banks.
+template <typename T>
+struct TileRow {
+  static constexpr int kShift = sizeof(T) == 4 ? 4 : 0;  // elements
+  static constexpr int kStride = kChunk + 8;             // elements per staged row (16-byte multiple)
+  __host__ __device__ static constexpr int pos(int t) { return t < kChunk / 2 ? t : t + kShift; }
+};
 
 // ---- element conversions ------------------------------------------------------------------
 
@@ -84,6 +95,19 @@ __device__ __forceinline__ void load_cached(const T* p, float (&x)[K]) {
   }
 }
 
+// K consecutive elements from shared memory (16/8/4-byte vector reads).
+template <typename T, int K>
+__device__ __forceinline__ void load_cached_smem(const T* p, float (&x)[K]) {
+  using R = RowVec<T, K>;
+#pragma unroll
+  for (int v = 0; v < R::kNV; ++v) {
+    typename R::V raw = reinterpret_cast<const typename R::V*>(p)[v];
+    const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+    for (int j = 0; j < R::kEPV; ++j) x[v * R::kEPV + j] = to_f32<T>(e[j]);
+  }
+}
+
 template <typename T, int K>
 __device__ __forceinline__ void store_stream(T* p, const float (&x)[K]) {
   using R = RowVec<T, K>;
@@ -132,6 +156,9 @@ __device__ __forceinline__ void load_bc_items(const T* p, int64_t stride, int64_
     for (int i = 0; i < K; ++i) x[i] = (t0 + i < L) ? to_f32<T>(__ldg(p + (t0 + i) * stride)) : 0.f;
   }
 }
+
+// Hint: bring the 128-byte line holding p into L2 (no register result).
+__device__ __forceinline__ void prefetch_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
 
 // ---- math ---------------------------------------------------------------------------------
 

@@ -50,6 +50,9 @@ struct BwdArgs {
 
 // Segments per channel (time-parallel lanes) the launchers pick for a call.
 int fwd_segments(int64_t rows);
+// Read and clear the device fault word of the forward / backward kernels (synchronous).
+cudaError_t read_fault_fwd(int* out);
+cudaError_t read_fault_bwd(int* out);
 int bwd_segments(int64_t rows);
 int bwd_cluster_size(int64_t tiles);
 

@@ -15,15 +15,22 @@
 //     forward saved at its start (chunk_states), so no seqlen x dstate history is materialised;
 //   * per state n: a forward shuffle scan rebuilds h inside the chunk (a_t kept in registers),
 //     a reverse shuffle scan of (a, gh) pairs carries gh across segments and chunks, then each
-//     lane walks its K steps backwards accumulating the gradients;
+//     lane walks its K steps backwards accumulating the gradients. The state loop is not unrolled
+//     (the body stays in the instruction cache); its per-state carries (gh entering the chunk and
+//     the lane's dA partial) live in shared memory;
 //   * dB/dC (sums over channels) are reduced deterministically: a reduce-scatter over the CW
 //     channel lanes of the warp (shuffles), a sum over the warps of the CTA (shared memory), a
 //     sum over the CTAs of a thread-block cluster (distributed shared memory), and finally a sum
 //     over clusters by the reduce kernel below. dA / dD / ddelta_bias leave the kernel as
 //     per-row partials and are summed over batch by the same reduce kernel.
+// Data movement: the B/C tile and the restart states of a chunk are staged in shared memory by
+// the bulk-copy engine one chunk ahead (double buffer, mbarrier completion); each lane's u /
+// delta / dout / z items are prefetched one chunk ahead into registers.
 #include <cooperative_groups.h>
 
 #include "scan.cuh"
+#include "segscan.cuh"
+#include "stage.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -36,21 +43,297 @@ constexpr int kRedFloats = kMaxState * 2 * kChunk;  // one CTA's dB|dC chunk par
 
 constexpr int ilog2(int v) { return v <= 1 ? 0 : 1 + ilog2(v / 2); }
 
+constexpr int kGroup = 4;  // states whose warp partials are summed together (one block barrier)
+
+template <typename TW, int CPC>
+struct BwdSmem {
+  TW bc[2][2][kMaxState][TileRow<TW>::kStride];   // [buf][B|C][n][staged t]
+  float hst[2][CPC][kMaxState];                   // [buf][channel][n]: state at the chunk start
+  float red[2][kBwdWarps][kGroup * 2 * kChunk];   // [group parity][warp]: dB|dC partials of a state group
+  float red_out[2][kRedFloats];                   // CTA sums of a chunk, double-buffered for cluster readers
+  float car[2][kMaxState][kBwdWarps * 32];        // [gh | dA partial][n][thread]
+  float A[CPC][kMaxState];
+  uint64_t bar[2];
+};
+
+template <typename TI, typename TW, int S, bool HAS_Z, bool STAGED, bool MASKED>
+__device__ __forceinline__ void bwd_chunk(const BwdArgs& a, BwdSmem<TW, kBwdWarps * (32 / S)>& sm, int buf, int k,
+                                          int64_t row, int64_t slice, int64_t cluster_idx, int cl_c, bool valid,
+                                          int lane, int warp, int c, int s, const TW* Bbase, const TW* Cbase,
+                                          float Dv, float bias, const TI* urow, const TI* drow, const TI* dorow,
+                                          const TI* zrow, float& dDacc, float& dbacc, int& rbuf,
+                                          cg::cluster_group& cluster) {
+  constexpr int K = kChunk / S;
+  constexpr int CW = 32 / S;
+  constexpr int R = ilog2(CW);
+  const ScanArgs& f = a.f;
+  const int64_t L = f.L;
+  const int N = (int)f.N;
+  const int64_t t0 = (int64_t)k * kChunk + s * K;
+
+  // The lane's items. u / delta / dout / z are read again at the end of the chunk (L1 hits)
+  // instead of being kept live through the state loop.
+  float dt[K], dtu[K], dy[K], gB[K], xA[K];
+  float y[HAS_Z ? K : 1];
+  float sdt = 0.f;
+  {
+    float uu[K], dl[K], dO[K], zz[K];
+    load_items<TI, K>(urow, t0, L, !MASKED, 0.f, uu);
+    load_items<TI, K>(drow, t0, L, !MASKED, 0.f, dl);
+    load_items<TI, K>(dorow, t0, L, !MASKED, 0.f, dO);
+    if constexpr (HAS_Z) load_items<TI, K>(zrow, t0, L, !MASKED, 0.f, zz);
+#pragma unroll
+    for (int i = 0; i < K; ++i) {
+      const float raw = dl[i] + bias;
+      float dti = f.softplus ? softplus_f(raw) : raw;
+      if (MASKED) dti = (t0 + i < L) ? dti : 0.f;
+      dt[i] = dti;
+      dtu[i] = dti * uu[i];
+      sdt += dti;
+      float dyi = dO[i];
+      if constexpr (HAS_Z) {
+        dyi = dO[i] * zz[i] * sigmoid_f(zz[i]);
+        y[i] = Dv * uu[i];
+      }
+      dy[i] = valid ? dyi : 0.f;
+      gB[i] = 0.f;
+      xA[i] = 0.f;
+    }
+  }
+
+  const TW* tB = &sm.bc[buf][0][0][0];
+  const TW* tC = &sm.bc[buf][1][0][0];
+
+  const int total4 = N * 2 * kChunk / 4;
+  int gpar = 0;
+#pragma unroll 1
+  for (int ng = 0; ng < N; ng += kGroup, gpar ^= 1) {
+    const int nend = min(ng + kGroup, N);
+#pragma unroll 1
+  for (int n = ng; n < nend; ++n) {
+    const float An = sm.A[cl_c][n];
+    const float A2n = An * kLog2e;
+    // Invalid (padding) lanes must stay finite: they contribute dy = 0 to the dB/dC sums, and
+    // 0 * NaN from an unwritten restart-state slot would poison them.
+    float hck = 0.f;
+    if (k > 0 && valid) {
+      if constexpr (STAGED)
+        hck = sm.hst[buf][cl_c][n];
+      else
+        hck = a.states[(row * f.nchunks + (k - 1)) * N + n];
+    }
+    float Bn[K], Cn[K], av[K], hs[K], bv[K];
+    if constexpr (STAGED) {
+      constexpr int kRS = TileRow<TW>::kStride;
+      const int tpos = TileRow<TW>::pos(s * K);
+      load_cached_smem<TW, K>(tB + n * kRS + tpos, Bn);
+      load_cached_smem<TW, K>(tC + n * kRS + tpos, Cn);
+    } else {
+      load_bc_items<TW, K>(Bbase + n * f.sBn, f.sBl, t0, L, MASKED ? false : (f.vec_bc != 0), Bn);
+      load_bc_items<TW, K>(Cbase + n * f.sCn, f.sCl, t0, L, MASKED ? false : (f.vec_bc != 0), Cn);
+    }
+#pragma unroll
+    for (int i = 0; i < K; ++i) {
+      av[i] = ex2(dt[i] * A2n);
+      bv[i] = dtu[i] * Bn[i];
+    }
+    if (MASKED) {
+#pragma unroll
+      for (int i = 0; i < K; ++i)
+        if (t0 + i >= L) av[i] = 1.f;
+    }
+    // -- forward: rebuild h inside the chunk
+    const float Aloc = seg_decay(An, sdt);  // this segment's total decay
+    float h0;
+    if constexpr (S > 1) {
+      float Al = Aloc, Bl = bv[0];
+#pragma unroll
+      for (int i = 1; i < K; ++i) Bl = fmaf(av[i], Bl, bv[i]);
+      scan_up<S>(s, Al, Bl);
+      float Ae = __shfl_up_sync(kFull, Al, 1, S);
+      float Be = __shfl_up_sync(kFull, Bl, 1, S);
+      if (s == 0) {
+        Ae = 1.f;
+        Be = 0.f;
+      }
+      h0 = fmaf(Ae, hck, Be);
+    } else {
+      h0 = hck;
+    }
+    {
+      float h = h0;
+#pragma unroll
+      for (int i = 0; i < K; ++i) {
+        h = fmaf(av[i], h, bv[i]);
+        hs[i] = h;
+        if constexpr (HAS_Z) y[i] = fmaf(h, Cn[i], y[i]);
+      }
+    }
+    // -- reverse: gh entering this lane's segment from later timesteps
+    const int tid = threadIdx.x;
+    const float gcn = sm.car[0][n][tid];
+    float gh, Ar = 1.f, Gr = 0.f;
+    if constexpr (S > 1) {
+      float Gl = 0.f;
+#pragma unroll
+      for (int i = K - 1; i >= 0; --i) Gl = av[i] * fmaf(dy[i], Cn[i], Gl);
+      Ar = Aloc;
+      Gr = Gl;
+      scan_down<S>(s, Ar, Gr);
+      float Ae = __shfl_down_sync(kFull, Ar, 1, S);
+      float Ge = __shfl_down_sync(kFull, Gr, 1, S);
+      if (s == S - 1) {
+        Ae = 1.f;
+        Ge = 0.f;
+      }
+      gh = fmaf(Ae, gcn, Ge);
+    } else {
+      gh = gcn;
+    }
+    float dAn = sm.car[1][n][tid];
+    float v[2 * K];  // [dB items | dC items] of this lane's channel
+#pragma unroll
+    for (int i = K - 1; i >= 0; --i) {
+      const float gg = fmaf(dy[i], Cn[i], gh);
+      v[K + i] = dy[i] * hs[i];
+      const float hp = i > 0 ? hs[i - 1] : h0;
+      const float xx = gg * (av[i] * hp);
+      dAn = fmaf(xx, dt[i], dAn);
+      xA[i] = fmaf(xx, An, xA[i]);
+      gB[i] = fmaf(gg, Bn[i], gB[i]);
+      v[i] = gg * dtu[i];
+      gh = gg * av[i];
+    }
+    // gh entering the previous chunk: the scanned map of the whole chunk applied to gcn
+    if constexpr (S > 1)
+      gh = __shfl_sync(kFull, fmaf(Ar, gcn, Gr), 0, S);
+    sm.car[0][n][tid] = gh;
+    sm.car[1][n][tid] = dAn;
+    // -- reduce-scatter dB|dC over the CW channel lanes holding the same timesteps
+    int io = 0;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int mask = S << r;
+      const bool upper = (lane & mask) != 0;
+      const int half = K >> r;
+#pragma unroll
+      for (int j = 0; j < half; ++j) {
+        const float send = upper ? v[j] : v[half + j];
+        const float keep = upper ? v[half + j] : v[j];
+        v[j] = keep + __shfl_xor_sync(kFull, send, mask);
+      }
+      if (r > 0 && upper) io += half;
+    }
+    const int q = (lane & S) ? 1 : 0;
+    *reinterpret_cast<float4*>(&sm.red[gpar][warp][((n - ng) * 2 + q) * kChunk + s * K + io]) =
+        make_float4(v[0], v[1], v[2], v[3]);
+  }
+    // -- sum the group's partials over the warps of the CTA (red is double-buffered by group
+    //    parity, so one barrier per group suffices)
+    __syncthreads();
+    {
+      float4* ro = reinterpret_cast<float4*>(sm.red_out[rbuf]) + ng * 2 * kChunk / 4;
+      const int g4 = (nend - ng) * 2 * kChunk / 4;
+      for (int f4 = threadIdx.x; f4 < g4; f4 += blockDim.x) {
+        float4 acc = reinterpret_cast<const float4*>(sm.red[gpar][0])[f4];
+#pragma unroll
+        for (int w = 1; w < kBwdWarps; ++w) {
+          const float4 o = reinterpret_cast<const float4*>(sm.red[gpar][w])[f4];
+          acc.x += o.x;
+          acc.y += o.y;
+          acc.z += o.z;
+          acc.w += o.w;
+        }
+        ro[f4] = acc;
+      }
+    }
+  }
+
+  // -- sum over the CTAs of the cluster
+  cluster.sync();
+  {
+    const int CL = (int)cluster.num_blocks();
+    const int crank = (int)cluster.block_rank();
+    const int per = (total4 + CL - 1) / CL;
+    const int lo = crank * per;
+    const int hi = min(total4, lo + per);
+    for (int f4 = lo + threadIdx.x; f4 < hi; f4 += blockDim.x) {
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int r = 0; r < CL; ++r) {
+        const float4* peer = reinterpret_cast<const float4*>(cluster.map_shared_rank(sm.red_out[rbuf], r));
+        const float4 o = peer[f4];
+        acc.x += o.x;
+        acc.y += o.y;
+        acc.z += o.z;
+        acc.w += o.w;
+      }
+      const int nq = f4 / (kChunk / 4);  // n * 2 + q
+      const int t4 = f4 % (kChunk / 4);
+      const int n = nq >> 1, q = nq & 1;
+      float* dst = a.part_bc + (((slice * a.clusters + cluster_idx) * 2 + q) * N + n) * a.Lpad +
+                   (int64_t)k * kChunk + t4 * 4;
+      *reinterpret_cast<float4*>(dst) = acc;
+    }
+  }
+  rbuf ^= 1;
+
+  // -- per-timestep gradients of this lane's K steps
+  float uu[K], dl[K], dO[K], zz[K];
+  load_items<TI, K>(urow, t0, L, !MASKED, 0.f, uu);
+  load_items<TI, K>(drow, t0, L, !MASKED, 0.f, dl);
+  if constexpr (HAS_Z) {
+    load_items<TI, K>(dorow, t0, L, !MASKED, 0.f, dO);
+    load_items<TI, K>(zrow, t0, L, !MASKED, 0.f, zz);
+  }
+  float du[K], dd[K];
+#pragma unroll
+  for (int i = 0; i < K; ++i) {
+    const float dsp = f.softplus ? sigmoid_f(dl[i] + bias) : 1.f;
+    const float ddt = (xA[i] + uu[i] * gB[i]) * dsp;
+    du[i] = Dv * dy[i] + dt[i] * gB[i];
+    dd[i] = ddt;
+    if (!MASKED || t0 + i < L) {
+      dbacc += ddt;
+      dDacc += dy[i] * uu[i];
+    }
+  }
+  if (valid) {
+    TI* durow = static_cast<TI*>(a.du) + row * L;
+    TI* ddrow = static_cast<TI*>(a.ddelta) + row * L;
+    if (MASKED) {
+      store_items<TI, K>(durow, t0, L, false, du);
+      store_items<TI, K>(ddrow, t0, L, false, dd);
+    } else {
+      store_stream<TI, K>(durow + t0, du);
+      store_stream<TI, K>(ddrow + t0, dd);
+    }
+    if constexpr (HAS_Z) {
+#pragma unroll
+      for (int i = 0; i < K; ++i) {
+        const float zs = sigmoid_f(zz[i]);
+        dd[i] = dO[i] * zs * (1.f + zz[i] * (1.f - zs)) * y[i];
+      }
+      TI* dzrow = static_cast<TI*>(a.dz) + row * L;
+      if (MASKED)
+        store_items<TI, K>(dzrow, t0, L, false, dd);
+      else
+        store_stream<TI, K>(dzrow + t0, dd);
+    }
+  }
+}
+
 template <typename TI, typename TW, int S, bool HAS_Z>
-__global__ void __launch_bounds__(kBwdWarps * 32, 2) scan_bwd_kernel(const BwdArgs a) {
+__global__ void __launch_bounds__(kBwdWarps * 32, 3) scan_bwd_kernel(const BwdArgs a) {
   constexpr int K = kChunk / S;
   constexpr int CW = 32 / S;
   constexpr int CPC = kBwdWarps * CW;
-  constexpr int R = ilog2(CW);  // reduce-scatter rounds over the channel lanes
   static_assert(S >= 2 && S <= 16, "segments per channel");
-  static_assert((2 * K) >> R == 4, "each lane ends the reduce-scatter with one float4");
-
-  __shared__ __align__(16) float red[kBwdWarps][kRedFloats];
-  __shared__ __align__(16) float red_out[2][kRedFloats];
+  static_assert((2 * K) >> ilog2(CW) == 4, "each lane ends the reduce-scatter with one float4");
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  BwdSmem<TW, CPC>& sm = *reinterpret_cast<BwdSmem<TW, CPC>*>(smem_raw);
 
   cg::cluster_group cluster = cg::this_cluster();
   const int CL = (int)cluster.num_blocks();
-  const int crank = (int)cluster.block_rank();
 
   const ScanArgs& f = a.f;
   const int lane = threadIdx.x & 31;
@@ -62,267 +345,113 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 2) scan_bwd_kernel(const BwdAr
   const int64_t b = slice / f.ngroups;
   const int64_t g = slice % f.ngroups;
   const int64_t cluster_idx = tile / CL;
-  const int64_t cig = tile * CPC + warp * CW + c;
+  const int64_t tile_c0 = tile * CPC;  // first channel (in group) of this CTA
+  const int64_t cig = tile_c0 + warp * CW + c;
   const bool valid = cig < f.dpg;
+  const int cl_c = valid ? warp * CW + c : 0;  // CTA slot whose staged rows this lane reads
   const int64_t d = g * f.dpg + (valid ? cig : 0);
   const int64_t row = b * f.dim + d;
   const int64_t L = f.L;
   const int N = (int)f.N;
-  const int nchunks = f.nchunks;
+  const int64_t nvalid = f.dpg - tile_c0 < CPC ? (f.dpg - tile_c0 > 0 ? f.dpg - tile_c0 : 0) : CPC;
 
   const TI* urow = static_cast<const TI*>(f.u) + row * L;
   const TI* drow = static_cast<const TI*>(f.delta) + row * L;
   const TI* zrow = HAS_Z ? static_cast<const TI*>(f.z) + row * L : nullptr;
   const TI* dorow = static_cast<const TI*>(a.dout) + row * L;
-  TI* durow = static_cast<TI*>(a.du) + row * L;
-  TI* ddrow = static_cast<TI*>(a.ddelta) + row * L;
-  TI* dzrow = HAS_Z ? static_cast<TI*>(a.dz) + row * L : nullptr;
   const TW* Bbase = static_cast<const TW*>(f.B) + b * f.sBb + g * f.sBg;
   const TW* Cbase = static_cast<const TW*>(f.C) + b * f.sCb + g * f.sCg;
-  const float* Arow = f.A + d * N;
   const float Dv = f.D ? f.D[d] : 0.f;
   const float bias = f.delta_bias ? f.delta_bias[d] : 0.f;
-  const bool vec_io = f.vec_io != 0;
-  const bool vec_bc = f.vec_bc != 0;
+  const bool staged = f.vec_bc != 0;
 
-  float gc[kMaxState];     // gh entering the current chunk from later timesteps
-  float dAacc[kMaxState];  // this lane's share of dA for its row
-#pragma unroll
-  for (int n = 0; n < kMaxState; ++n) {
-    gc[n] = (valid && a.dlast != nullptr && n < N) ? a.dlast[row * N + n] : 0.f;
-    dAacc[n] = 0.f;
+  // per-lane carries and the channels' A rows
+  for (int n = 0; n < N; ++n) {
+    sm.car[0][n][threadIdx.x] = (valid && a.dlast != nullptr) ? a.dlast[row * N + n] : 0.f;
+    sm.car[1][n][threadIdx.x] = 0.f;
   }
+  for (int i = threadIdx.x; i < CPC * N; i += blockDim.x) {
+    const int ch = i / N, n = i % N;
+    const int64_t dd = g * f.dpg + (tile_c0 + ch < f.dpg ? tile_c0 + ch : 0);
+    sm.A[ch][n] = f.A[dd * N + n];
+  }
+  if (staged && threadIdx.x == 0) {
+    mbar_init(&sm.bar[0], 1);
+    mbar_init(&sm.bar[1], 1);
+    mbar_fence_init();
+  }
+  __syncthreads();
+
+  // first row (global index) of this CTA's channels, for the restart-state copies
+  const int64_t row_c0 = b * f.dim + g * f.dpg + tile_c0;
+  auto issue = [&](int k, int buf) {  // warp 0: B/C tile and restart states of chunk k
+    constexpr uint32_t half_bytes = kChunk / 2 * sizeof(TW);
+    constexpr uint32_t st_bytes = kMaxState * sizeof(float);
+    const bool with_states = k > 0 && N == kMaxState;
+    const int nst = with_states ? (int)nvalid : 0;
+    if (lane == 0) mbar_arrive_expect_tx(&sm.bar[buf], 4 * N * half_bytes + nst * st_bytes);
+    __syncwarp();
+    fence_proxy_async();
+    for (int j = lane; j < 4 * N + nst; j += 32) {
+      if (j < 4 * N) {  // B/C rows in two halves (TileRow layout)
+        const int r = j >> 1, hf = j & 1;
+        const bool isC = r >= N;
+        const int n = isC ? r - N : r;
+        const TW* src = (isC ? Cbase + n * f.sCn : Bbase + n * f.sBn) + (int64_t)k * kChunk + hf * (kChunk / 2);
+        bulk_g2s(&sm.bc[buf][isC ? 1 : 0][n][TileRow<TW>::pos(hf * (kChunk / 2))], src, half_bytes, &sm.bar[buf]);
+      } else {
+        const int ch = j - 4 * N;
+        bulk_g2s(&sm.hst[buf][ch][0], a.states + ((row_c0 + ch) * f.nchunks + (k - 1)) * kMaxState, st_bytes,
+                 &sm.bar[buf]);
+      }
+    }
+    if (k > 0 && N != kMaxState) {  // restart states not 64-byte rows: plain loads (all lanes of warp 0)
+      for (int i = lane; i < (int)nvalid * N; i += 32) {
+        const int ch = i / N, n = i % N;
+        sm.hst[buf][ch][n] = a.states[((row_c0 + ch) * f.nchunks + (k - 1)) * N + n];
+      }
+    }
+  };
+
   float dDacc = 0.f, dbacc = 0.f;
-  int buf = 0;
+  int rbuf = 0;
+  const bool vec_io = f.vec_io != 0;
+  const int nfull = (vec_io && staged) ? (int)(L / kChunk) : 0;
 
-  for (int k = nchunks - 1; k >= 0; --k) {
-    const int64_t t0 = (int64_t)k * kChunk + s * K;
-    const bool tail = t0 + K > L;
-    float dt[K], dtu[K], dy[K], uu[K], dsp[K], gB[K], xA[K];
-    float dzc[HAS_Z ? K : 1], y[HAS_Z ? K : 1];
-    {
-      float dl[K], dO[K];
-      load_items<TI, K>(urow, t0, L, vec_io, 0.f, uu);
-      load_items<TI, K>(drow, t0, L, vec_io, 0.f, dl);
-      load_items<TI, K>(dorow, t0, L, vec_io, 0.f, dO);
-      float zz[HAS_Z ? K : 1];
-      if constexpr (HAS_Z) load_items<TI, K>(zrow, t0, L, vec_io, 0.f, zz);
-#pragma unroll
-      for (int i = 0; i < K; ++i) {
-        const bool in = t0 + i < L;
-        const float raw = dl[i] + bias;
-        const float sp = f.softplus ? softplus_f(raw) : raw;
-        dsp[i] = f.softplus ? sigmoid_f(raw) : 1.f;
-        dt[i] = in ? sp : 0.f;
-        dtu[i] = dt[i] * uu[i];
-        float dyi = dO[i];
-        if constexpr (HAS_Z) {
-          const float zs = sigmoid_f(zz[i]);
-          dyi = dO[i] * zz[i] * zs;
-          dzc[i] = dO[i] * zs * (1.f + zz[i] * (1.f - zs));
-          y[i] = Dv * uu[i];
-        }
-        dy[i] = valid ? dyi : 0.f;
-        gB[i] = 0.f;
-        xA[i] = 0.f;
-      }
+  // The partial last chunk (and every chunk of an unaligned row) goes first: masked, direct loads.
+  for (int k = f.nchunks - 1; k >= nfull; --k) {
+    bwd_chunk<TI, TW, S, HAS_Z, false, true>(a, sm, 0, k, row, slice, cluster_idx, cl_c, valid, lane, warp, c, s,
+                                             Bbase, Cbase, Dv, bias, urow, drow, dorow, zrow, dDacc, dbacc, rbuf,
+                                             cluster);
+  }
+  // Full chunks, last to first: B/C + restart states staged one chunk ahead by the bulk-copy
+  // engine; the lane's own rows of the next chunk are prefetched into L2.
+  if (nfull > 0 && warp == 0) issue(nfull - 1, (nfull - 1) & 1);
+  for (int k = nfull - 1; k >= 0; --k) {
+    const int buf = k & 1;
+    if (k > 0) {
+      const int64_t t1 = (int64_t)(k - 1) * kChunk + s * K;
+      prefetch_l2(urow + t1);
+      prefetch_l2(drow + t1);
+      prefetch_l2(dorow + t1);
+      if constexpr (HAS_Z) prefetch_l2(zrow + t1);
+      if (warp == 0) issue(k - 1, buf ^ 1);
     }
-
-#pragma unroll
-    for (int n = 0; n < kMaxState; ++n) {
-      if (n < N) {
-        const float An = Arow[n];
-        const float A2n = An * kLog2e;
-        const float hck = k > 0 ? a.states[(row * nchunks + (k - 1)) * N + n] : 0.f;
-        float Bn[K], Cn[K], av[K], hs[K];
-        load_bc_items<TW, K>(Bbase + n * f.sBn, f.sBl, t0, L, vec_bc, Bn);
-        load_bc_items<TW, K>(Cbase + n * f.sCn, f.sCl, t0, L, vec_bc, Cn);
-#pragma unroll
-        for (int i = 0; i < K; ++i) av[i] = ex2(dt[i] * A2n);
-        if (tail) {
-#pragma unroll
-          for (int i = 0; i < K; ++i)
-            if (t0 + i >= L) av[i] = 1.f;
-        }
-        // -- forward: rebuild h inside the chunk
-        float h0, Aloc = av[0];
-        if constexpr (S > 1) {
-          float Al = av[0], Bl = dtu[0] * Bn[0];
-#pragma unroll
-          for (int i = 1; i < K; ++i) {
-            Bl = fmaf(av[i], Bl, dtu[i] * Bn[i]);
-            Al *= av[i];
-          }
-          Aloc = Al;
-#pragma unroll
-          for (int off = 1; off < S; off <<= 1) {
-            const float Ap = __shfl_up_sync(kFull, Al, off, S);
-            const float Bp = __shfl_up_sync(kFull, Bl, off, S);
-            if (s >= off) {
-              Bl = fmaf(Al, Bp, Bl);
-              Al *= Ap;
-            }
-          }
-          float Ae = __shfl_up_sync(kFull, Al, 1, S);
-          float Be = __shfl_up_sync(kFull, Bl, 1, S);
-          if (s == 0) {
-            Ae = 1.f;
-            Be = 0.f;
-          }
-          h0 = fmaf(Ae, hck, Be);
-        } else {
-          h0 = hck;
-        }
-        {
-          float h = h0;
-#pragma unroll
-          for (int i = 0; i < K; ++i) {
-            h = fmaf(av[i], h, dtu[i] * Bn[i]);
-            hs[i] = h;
-            if constexpr (HAS_Z) y[i] = fmaf(h, Cn[i], y[i]);
-          }
-        }
-        // -- reverse: gh entering this lane's segment from later timesteps
-        float gh;
-        if constexpr (S > 1) {
-          float Gl = 0.f;
-#pragma unroll
-          for (int i = K - 1; i >= 0; --i) Gl = av[i] * fmaf(dy[i], Cn[i], Gl);
-          float Ar = Aloc, Gr = Gl;
-#pragma unroll
-          for (int off = 1; off < S; off <<= 1) {
-            const float An_ = __shfl_down_sync(kFull, Ar, off, S);
-            const float Gn_ = __shfl_down_sync(kFull, Gr, off, S);
-            if (s + off < S) {
-              Gr = fmaf(Ar, Gn_, Gr);
-              Ar *= An_;
-            }
-          }
-          float Ae = __shfl_down_sync(kFull, Ar, 1, S);
-          float Ge = __shfl_down_sync(kFull, Gr, 1, S);
-          if (s == S - 1) {
-            Ae = 1.f;
-            Ge = 0.f;
-          }
-          gh = fmaf(Ae, gc[n], Ge);
-        } else {
-          gh = gc[n];
-        }
-        float v[2 * K];  // [dB items | dC items] of this lane's channel
-#pragma unroll
-        for (int i = K - 1; i >= 0; --i) {
-          const float gg = fmaf(dy[i], Cn[i], gh);
-          v[K + i] = dy[i] * hs[i];
-          const float hp = i > 0 ? hs[i - 1] : h0;
-          const float x = gg * (av[i] * hp);
-          dAacc[n] = fmaf(x, dt[i], dAacc[n]);
-          xA[i] = fmaf(x, An, xA[i]);
-          gB[i] = fmaf(gg, Bn[i], gB[i]);
-          v[i] = gg * dtu[i];
-          gh = gg * av[i];
-        }
-        if constexpr (S > 1)
-          gc[n] = __shfl_sync(kFull, gh, 0, S);
-        else
-          gc[n] = gh;
-        // -- reduce-scatter dB|dC over the CW channel lanes holding the same timesteps
-        int io = 0;
-#pragma unroll
-        for (int r = 0; r < R; ++r) {
-          const int mask = S << r;
-          const bool upper = (lane & mask) != 0;
-          const int half = K >> r;  // values kept after this round (2K >> (r + 1))
-#pragma unroll
-          for (int j = 0; j < half; ++j) {
-            const float send = upper ? v[j] : v[half + j];
-            const float keep = upper ? v[half + j] : v[j];
-            v[j] = keep + __shfl_xor_sync(kFull, send, mask);
-          }
-          if (r > 0 && upper) io += half;
-        }
-        const int q = (lane & S) ? 1 : 0;
-        *reinterpret_cast<float4*>(&red[warp][(n * 2 + q) * kChunk + s * K + io]) =
-            make_float4(v[0], v[1], v[2], v[3]);
-      }
-    }
-
-    // -- sum over the warps of the CTA, then over the CTAs of the cluster
-    __syncthreads();
-    const int total4 = N * 2 * kChunk / 4;
-    {
-      float4* ro = reinterpret_cast<float4*>(red_out[buf]);
-      for (int f4 = threadIdx.x; f4 < total4; f4 += blockDim.x) {
-        float4 acc = reinterpret_cast<const float4*>(red[0])[f4];
-#pragma unroll
-        for (int w = 1; w < kBwdWarps; ++w) {
-          const float4 o = reinterpret_cast<const float4*>(red[w])[f4];
-          acc.x += o.x;
-          acc.y += o.y;
-          acc.z += o.z;
-          acc.w += o.w;
-        }
-        ro[f4] = acc;
-      }
-    }
-    cluster.sync();
-    {
-      const int per = (total4 + CL - 1) / CL;
-      const int lo = crank * per;
-      const int hi = min(total4, lo + per);
-      for (int f4 = lo + threadIdx.x; f4 < hi; f4 += blockDim.x) {
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int r = 0; r < CL; ++r) {
-          const float4* peer = reinterpret_cast<const float4*>(cluster.map_shared_rank(red_out[buf], r));
-          const float4 o = peer[f4];
-          acc.x += o.x;
-          acc.y += o.y;
-          acc.z += o.z;
-          acc.w += o.w;
-        }
-        const int nq = f4 / (kChunk / 4);  // n * 2 + q
-        const int t4 = f4 % (kChunk / 4);
-        const int n = nq >> 1, q = nq & 1;
-        float* dst = a.part_bc + (((slice * a.clusters + cluster_idx) * 2 + q) * N + n) * a.Lpad +
-                     (int64_t)k * kChunk + t4 * 4;
-        *reinterpret_cast<float4*>(dst) = acc;
-      }
-    }
-    buf ^= 1;
-
-    // -- per-timestep gradients of this lane's K steps
-    {
-      float du[K], dd[K];
-#pragma unroll
-      for (int i = 0; i < K; ++i) {
-        const float ddt = (xA[i] + uu[i] * gB[i]) * dsp[i];
-        du[i] = Dv * dy[i] + dt[i] * gB[i];
-        dd[i] = ddt;
-        if (t0 + i < L) {
-          dbacc += ddt;
-          dDacc += dy[i] * uu[i];
-        }
-      }
-      if (valid) {
-        store_items<TI, K>(durow, t0, L, vec_io, du);
-        store_items<TI, K>(ddrow, t0, L, vec_io, dd);
-        if constexpr (HAS_Z) {
-#pragma unroll
-          for (int i = 0; i < K; ++i) dd[i] = dzc[i] * y[i];
-          store_items<TI, K>(dzrow, t0, L, vec_io, dd);
-        }
-      }
-    }
+    // Uses of bar[buf], from the last chunk downwards: chunk k is use number (nfull-1-k)/2.
+    mbar_wait(&sm.bar[buf], (uint32_t)(((nfull - 1 - k) >> 1) & 1));
+    bwd_chunk<TI, TW, S, HAS_Z, true, false>(a, sm, buf, k, row, slice, cluster_idx, cl_c, valid, lane, warp, c, s,
+                                             Bbase, Cbase, Dv, bias, urow, drow, dorow, zrow, dDacc, dbacc, rbuf,
+                                             cluster);
+    // bwd_chunk ends with cluster.sync() after its last shared-memory read of this buffer, so the
+    // next iteration may refill it.
   }
 
   // -- per-row partials of dA / dD / ddelta_bias: sum the S segment lanes of the channel
+  for (int n = 0; n < N; ++n) {
+    float v = sm.car[1][n][threadIdx.x];
 #pragma unroll
-  for (int n = 0; n < kMaxState; ++n) {
-    if (n < N) {
-      float v = dAacc[n];
-#pragma unroll
-      for (int off = S / 2; off > 0; off >>= 1) v += __shfl_xor_sync(kFull, v, off, S);
-      if (valid && s == 0) a.part_A[row * N + n] = v;
-    }
+    for (int off = S / 2; off > 0; off >>= 1) v += __shfl_xor_sync(kFull, v, off, S);
+    if (valid && s == 0) a.part_A[row * N + n] = v;
   }
 #pragma unroll
   for (int off = S / 2; off > 0; off >>= 1) {
@@ -343,10 +472,14 @@ cudaError_t launch_typed(BwdArgs a, int cluster, cudaStream_t stream) {
   const int64_t tiles = (a.f.dpg + CPC - 1) / CPC;
   a.f.tiles = (int)(((tiles + cluster - 1) / cluster) * cluster);
   a.clusters = a.f.tiles / cluster;
+  constexpr size_t smem = sizeof(BwdSmem<TW, CPC>);
+  auto kern = a.f.z != nullptr ? scan_bwd_kernel<TI, TW, S, true> : scan_bwd_kernel<TI, TW, S, false>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(a.f.tiles * a.f.batch * a.f.ngroups));
   cfg.blockDim = dim3(kBwdWarps * 32);
-  cfg.dynamicSmemBytes = 0;
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -355,8 +488,7 @@ cudaError_t launch_typed(BwdArgs a, int cluster, cudaStream_t stream) {
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (a.f.z != nullptr) return cudaLaunchKernelEx(&cfg, scan_bwd_kernel<TI, TW, S, true>, a);
-  return cudaLaunchKernelEx(&cfg, scan_bwd_kernel<TI, TW, S, false>, a);
+  return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
 template <typename TI, typename TW>
@@ -368,9 +500,9 @@ cudaError_t launch_seg(const BwdArgs& a, int cluster, cudaStream_t stream) {
 // ---- reduction of the partials ---------------------------------------------------------------
 
 template <typename TO>
-__global__ void scan_bwd_reduce_kernel(const BwdArgs a, TO* dB, TO* dC, int64_t osb, int64_t osg,
-                                       int64_t osn, int64_t osl, float* dA, float* dD, float* db,
-                                       int64_t n_bc4, int64_t n_A, int64_t n_D) {
+__global__ void scan_bwd_reduce_kernel(const BwdArgs a, TO* dB, TO* dC, int64_t osb, int64_t osg, int64_t osn,
+                                       int64_t osl, float* dA, float* dD, float* db, int64_t n_bc4, int64_t n_A,
+                                       int64_t n_D) {
   const int64_t N = a.f.N, L = a.f.L, Lpad = a.Lpad;
   const int64_t L4 = Lpad / 4;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -420,6 +552,8 @@ __global__ void scan_bwd_reduce_kernel(const BwdArgs a, TO* dB, TO* dC, int64_t 
 
 int bwd_segments(int64_t rows) { return rows >= 4096 ? 8 : 16; }
 
+cudaError_t read_fault_bwd(int* out) { return read_fault_word(out); }
+
 int bwd_cluster_size(int64_t tiles) {
   if (tiles >= 8) return 8;
   if (tiles >= 4) return 4;
@@ -427,8 +561,7 @@ int bwd_cluster_size(int64_t tiles) {
   return 1;
 }
 
-cudaError_t launch_scan_bwd(const BwdArgs& a, int io_dtype, int bc_dtype, int cluster,
-                            cudaStream_t stream) {
+cudaError_t launch_scan_bwd(const BwdArgs& a, int io_dtype, int bc_dtype, int cluster, cudaStream_t stream) {
   if (a.f.batch == 0 || a.f.dim == 0) return cudaSuccess;
   if (io_dtype == MB200_F32) return launch_seg<float, float>(a, cluster, stream);
   if (io_dtype == MB200_BF16) {
@@ -439,10 +572,9 @@ cudaError_t launch_scan_bwd(const BwdArgs& a, int io_dtype, int bc_dtype, int cl
   return launch_seg<__half, float>(a, cluster, stream);
 }
 
-cudaError_t launch_scan_bwd_reduce_strided(const BwdArgs& a, void* dB, void* dC, int dbc_dtype,
-                                           int64_t osb, int64_t osg, int64_t osn, int64_t osl,
-                                           float* dA, float* dD, float* db, bool batch_partials,
-                                           cudaStream_t stream) {
+cudaError_t launch_scan_bwd_reduce_strided(const BwdArgs& a, void* dB, void* dC, int dbc_dtype, int64_t osb,
+                                           int64_t osg, int64_t osn, int64_t osl, float* dA, float* dD, float* db,
+                                           bool batch_partials, cudaStream_t stream) {
   const int64_t slices = a.f.batch * a.f.ngroups;
   const int64_t n_bc4 = slices * 2 * a.f.N * (a.Lpad / 4);
   const int64_t n_A = batch_partials ? 0 : a.f.dim * a.f.N;

@@ -104,6 +104,7 @@ SIGNATURES = {
     "mb200_status_string": ([ctypes.c_int], ctypes.c_char_p),
     "mb200_version": ([], ctypes.c_int),
     "mb200_last_launch_count": ([], ctypes.c_int),
+    "mb200_device_fault": ([ctypes.POINTER(ctypes.c_int)], ctypes.c_int),
 }
 
 
@@ -131,6 +132,13 @@ def check(status: int, what: str) -> None:
     if status != OK:
         exc = _STATUS_EXC.get(status, RuntimeError)
         raise exc(f"{what}: {status_string(status)} (status {status})")
+
+
+def device_fault() -> int:
+    """Read and clear the kernels' device-side fault word (0 = none). Synchronises the device."""
+    v = ctypes.c_int(0)
+    check(lib.mb200_device_fault(ctypes.byref(v)), "mb200_device_fault")
+    return v.value
 
 
 def last_launch_count() -> int:

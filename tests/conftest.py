@@ -23,3 +23,16 @@ def pytest_collection_modifyitems(config, items):
     for item in items:
         if "gpu" in item.keywords:
             item.add_marker(skip)
+
+
+@pytest.fixture(autouse=True)
+def _no_device_fault(request):
+    """GPU tests: no kernel may have recorded a fault (a bounded wait that gave up)."""
+    yield
+    if "gpu" in request.keywords:
+        import torch
+
+        if torch.cuda.is_available():
+            from mamba_cpu_b200 import _lib
+
+            assert _lib.device_fault() == 0, "a kernel recorded a device-side fault"

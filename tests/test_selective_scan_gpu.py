@@ -270,3 +270,42 @@ def test_config2_fwd_bwd_full_size():
     for k, gk in GRAD_OF.items():
         w = want[gk].reshape(inp[k].shape)
         assert_close(leaves[k].grad, w, 1e-4, 1e-5, k, max_frac=fracs.get(k, 1e-4), norm_tol=1e-5)
+
+
+@pytest.mark.parametrize("ngroups,seqlen", [(1, 200), (2, 64), (1, 37)])
+def test_reference_abi_mirror_f32(ngroups, seqlen):
+    """mb200_selective_scan_{fwd,bwd}_f32 take the reference binding's exact arguments
+    (csrc/bindings.cpp:23-84): fp32, B/C as (batch, ngroups, seqlen, dstate), per-batch partials."""
+    from mamba_cpu_b200 import _lib
+
+    b, d, n = 2, 32, 16
+    inp = make_inputs(b, d, seqlen, n, ngroups, True, True, True, torch.float32)
+    g = to_cuda(inp)
+    Bk = g["B"].transpose(-1, -2).contiguous()  # (b, g, l, n)
+    Ck = g["C"].transpose(-1, -2).contiguous()
+    out = torch.empty(b, d, seqlen, device="cuda")
+    last = torch.empty(b, d, n, device="cuda")
+    P = lambda t: None if t is None else t.data_ptr()  # noqa: E731
+    st = _lib.lib.mb200_selective_scan_fwd_f32(P(g["u"]), P(g["delta"]), P(g["A"]), P(Bk), P(Ck), P(g["D"]), P(g["z"]),
+                                               P(g["delta_bias"]), P(out), P(last), b, d, seqlen, n, ngroups, 1,
+                                               None)
+    assert st == 0
+    o64, l64 = f64.scan_fwd(*oracle_args(inp), delta_softplus=True)
+    assert_close(out, o64, 1e-5, 1e-5, "out")
+    assert_close(last, l64, 1e-5, 1e-5, "last")
+    dout = torch.randn(b, d, seqlen, generator=torch.Generator().manual_seed(5))
+    du, ddelta, dz = (torch.empty(b, d, seqlen, device="cuda") for _ in range(3))
+    dA_part = torch.empty(b, d, n, device="cuda")
+    dB, dC = torch.zeros_like(Bk), torch.zeros_like(Ck)
+    dD_part, db_part = torch.empty(b, d, device="cuda"), torch.empty(b, d, device="cuda")
+    st = _lib.lib.mb200_selective_scan_bwd_f32(
+        P(g["u"]), P(g["delta"]), P(g["A"]), P(Bk), P(Ck), P(g["D"]), P(g["z"]), P(g["delta_bias"]),
+        P(dout.cuda()), None, P(du), P(ddelta), P(dA_part), P(dB), P(dC), P(dD_part), P(dz), P(db_part),
+        b, d, seqlen, n, ngroups, 1, None)
+    assert st == 0
+    want = f64.scan_bwd(*oracle_args(inp), True, dout)
+    for got, k in ((du, "du"), (ddelta, "ddelta"), (dz, "dz"), (dA_part.sum(0), "dA"), (dD_part.sum(0), "dD"),
+                   (db_part.sum(0), "ddelta_bias"), (dB.transpose(-1, -2), "dB"), (dC.transpose(-1, -2), "dC")):
+        w = want[k].reshape(got.shape)
+        scale = max(1.0, float(np.abs(w).max()))
+        assert_close(np64(got) / scale, w / scale, 1e-4, 1e-4, k)
