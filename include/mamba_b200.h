@@ -45,6 +45,7 @@ extern "C" {
 #define MB200_ERR_UNSUPPORTED 5  /* a valid request outside this build (e.g. dstate > 16) */
 #define MB200_ERR_WORKSPACE 6    /* workspace NULL or smaller than *_workspace_size */
 #define MB200_ERR_CUDA 7         /* a CUDA runtime call failed (launch error, allocation) */
+#define MB200_ERR_SCRATCH_LIMIT 8 /* needs more than the no-allocation entry point's static scratch */
 
 /* ---- dtype codes ------------------------------------------------------------------------- */
 #define MB200_F32 0
@@ -142,6 +143,23 @@ MB200_API size_t mb200_selective_scan_bwd_workspace_size(const mb200_scan_bwd_pa
  * (src/mamba_cpu/ops/selective_scan_interface.py:48-87). */
 MB200_API int mb200_selective_scan_bwd(const mb200_scan_bwd_params* p, void* workspace,
                                        size_t workspace_bytes, void* stream);
+
+/* Size of the static device scratch behind mb200_selective_scan_bwd_noalloc (16 MiB). */
+#define MB200_NOALLOC_SCRATCH_BYTES ((size_t)16 << 20)
+
+/* Backward selective scan that allocates nothing, for callers that can neither allocate device
+ * memory nor provide a workspace (e.g. a host framework that owns all device memory and forbids
+ * allocation inside its execute callbacks). This entry point has no counterpart in the reference.
+ * It runs mb200_selective_scan_bwd with a workspace carved from a static device array of
+ * MB200_NOALLOC_SCRATCH_BYTES that every GPU loading this library holds until the process exits.
+ * Requests whose mb200_selective_scan_bwd_workspace_size exceeds that limit return
+ * MB200_ERR_SCRATCH_LIMIT before anything is enqueued (with fwd.chunk_states given, about a
+ * batch 4 x dim 1536 x seqlen 1024 problem fits; without it roughly half that).
+ * The first call on each device resolves the array's device address (a runtime query) and should
+ * come before any stream capture on that device. All calls on a device share the array: calls
+ * whose GPU work may overlap (other streams, other host threads) race and must be serialised by
+ * the caller. Nothing in the array needs clearing between calls. */
+MB200_API int mb200_selective_scan_bwd_noalloc(const mb200_scan_bwd_params* p, void* stream);
 
 /* Exact mirror of the reference binding `selective_scan_fwd_f32` (csrc/bindings.cpp:23-45):
  * same argument order and meaning -- float32 everywhere, B/C in the reference kernel's

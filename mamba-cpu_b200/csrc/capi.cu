@@ -419,6 +419,9 @@ MB200_API const char* mb200_status_string(int status) {
       return "workspace missing, misaligned or smaller than the *_workspace_size result";
     case MB200_ERR_CUDA:
       return "a CUDA runtime call failed";
+    case MB200_ERR_SCRATCH_LIMIT:
+      return "request needs more scratch than the no-allocation entry point's static buffer "
+             "(MB200_NOALLOC_SCRATCH_BYTES); use mb200_selective_scan_bwd with a workspace";
     default:
       return "unknown status";
   }

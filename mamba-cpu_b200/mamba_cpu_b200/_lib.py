@@ -33,6 +33,7 @@ _STATUS_EXC = {
     5: NotImplementedError,
     6: RuntimeError,  # workspace
     7: RuntimeError,  # CUDA
+    8: ValueError,  # exceeds the no-allocation entry point's static scratch
 }
 
 _vp = ctypes.c_void_p
@@ -93,6 +94,7 @@ SIGNATURES = {
     "mb200_selective_scan_fwd": ([ctypes.POINTER(ScanFwdParams), _vp], ctypes.c_int),
     "mb200_selective_scan_bwd_workspace_size": ([ctypes.POINTER(ScanBwdParams)], ctypes.c_size_t),
     "mb200_selective_scan_bwd": ([ctypes.POINTER(ScanBwdParams), _vp, ctypes.c_size_t, _vp], ctypes.c_int),
+    "mb200_selective_scan_bwd_noalloc": ([ctypes.POINTER(ScanBwdParams), _vp], ctypes.c_int),
     "mb200_selective_scan_fwd_f32": ([_vp] * 10 + [_i64] * 5 + [ctypes.c_int, _vp], ctypes.c_int),
     "mb200_selective_scan_bwd_f32": ([_vp] * 18 + [_i64] * 5 + [ctypes.c_int, _vp], ctypes.c_int),
     "mb200_causal_conv1d_fwd": ([ctypes.POINTER(Conv1dParams), _vp], ctypes.c_int),
