@@ -67,12 +67,17 @@ def load_peak():
 
 def load_traffic(config):
     """Per-element DRAM traffic of the dominant kernel from the committed ncu summary, if any."""
-    path = os.path.join(ROOT, "profiles", "traffic.json")
+    path = os.path.join(ROOT, "profiles", "roofline_traffic.txt")
+    out = {}
     try:
         with open(path) as f:
-            return json.load(f).get(config)
-    except Exception:
+            for line in f:
+                parts = line.split()
+                if len(parts) == 3 and not line.startswith("#") and parts[0] == config:
+                    out[parts[1]] = float(parts[2])
+    except OSError:
         return None
+    return out or None
 
 
 class Clocks:
