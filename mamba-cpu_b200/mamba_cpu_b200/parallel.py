@@ -2,19 +2,24 @@
 
 Every (batch, channel) row of the scan is an independent recurrence (mamba-cpu
 csrc/selective_scan.cpp:320-324), so ranks can each own a contiguous slice of the channels with
-u, delta, z, out, A, D, delta_bias (and their gradients) sharded along ``dim`` and B, C replicated.
-The forward needs no communication. In the backward, dB and dC are sums over ALL channels of a
-group, so each rank's partial sums are combined with one all-reduce(SUM) of the fp32 [dB | dC]
-buffer per call. With ngroups > 1 a shard must not split a group (checked by
-:func:`shard_bounds`).
+u, delta, z, out, A, D, delta_bias (and their gradients) sharded along ``dim``. B and C are
+replicated: a rank passes the B / C groups its channels read (:func:`bc_groups`; all of B / C when
+ngroups = 1). The forward needs no communication. In the backward, dB and dC are sums over ALL
+channels of a group, so the partial sums of the ranks that share a group are combined with one
+all-reduce(SUM) of the fp32 [dB | dC] buffer per call, over :func:`new_reduce_group`'s process
+group. A shard holds whole groups or a part of one group, never a part of two (checked by
+:func:`shard_bounds`); a rank that holds whole groups needs no collective at all.
 
 Usage (one process per GPU, ``torch.distributed`` initialised with the NCCL backend)::
 
     from mamba_cpu_b200 import selective_scan_fn, parallel
     lo, hi = parallel.shard_bounds(dim, ngroups, rank, world)
+    glo, ghi = parallel.bc_groups(dim, ngroups, rank, world)      # B, C: (b, g, n, l)
+    group = parallel.new_reduce_group(dim, ngroups, rank, world)  # collective: every rank calls it
     with parallel.channel_sharded(group):
-        out = selective_scan_fn(u[:, lo:hi], delta[:, lo:hi], A[lo:hi], B, C, D[lo:hi], ...)
-        out.backward(...)         # dB / dC arrive all-reduced on every rank
+        out = selective_scan_fn(u[:, lo:hi], delta[:, lo:hi], A[lo:hi], B[:, glo:ghi], C[:, glo:ghi],
+                                D[lo:hi], ...)
+        out.backward(...)         # dB / dC arrive summed over the ranks sharing the groups
 
 The group is captured when the forward runs, so the backward may run outside the context.
 """
@@ -54,6 +59,42 @@ def shard_bounds(dim: int, ngroups: int, rank: int, world: int) -> tuple[int, in
     if not (per % dpg == 0 or dpg % per == 0):
         raise ValueError(f"a shard of {per} channels would split a group of {dpg} channels")
     return rank * per, (rank + 1) * per
+
+
+def bc_groups(dim: int, ngroups: int, rank: int, world: int) -> tuple[int, int]:
+    """Range [glo, ghi) of the B / C groups that ``rank``'s channels read."""
+    lo, hi = shard_bounds(dim, ngroups, rank, world)
+    dpg = dim // ngroups
+    return lo // dpg, (hi - 1) // dpg + 1
+
+
+def reduce_ranks(dim: int, ngroups: int, rank: int, world: int) -> list[int]:
+    """The ranks whose channels read the same B / C groups as ``rank`` (``rank`` included): their
+    partial dB / dC are summed. A single rank when shards hold whole groups."""
+    mine = bc_groups(dim, ngroups, rank, world)
+    return [r for r in range(world) if bc_groups(dim, ngroups, r, world) == mine]
+
+
+def new_reduce_group(dim: int, ngroups: int, rank: int, world: int):
+    """Process group over :func:`reduce_ranks` for ``rank`` (None when that is ``rank`` alone).
+
+    Creates the process groups of ALL rank sets with ``torch.distributed.new_group``, which every
+    rank of the default group must call in the same order, so every rank calls this function."""
+    import torch.distributed as dist
+
+    sets = []
+    for r in range(world):
+        s = reduce_ranks(dim, ngroups, r, world)
+        if s not in sets:
+            sets.append(s)
+    if all(len(s) == world for s in sets):
+        return dist.group.WORLD if world > 1 else None
+    mine = None
+    for s in sets:
+        pg = dist.new_group(ranks=s) if len(s) > 1 else None
+        if rank in s:
+            mine = pg
+    return mine
 
 
 def all_reduce_bc(dB: torch.Tensor, dC: torch.Tensor, group, async_op: bool = False):
