@@ -169,11 +169,31 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-// torch.nn.functional.softplus with its default threshold 20 (mamba-cpu selective_scan.cpp:45).
-__device__ __forceinline__ float softplus_f(float x) { return x <= 20.f ? log1pf(__expf(x)) : x; }
+// torch.nn.functional.softplus with its default threshold 20 (mamba-cpu selective_scan.cpp:45:
+// x for x > 20, else log(1 + e^x)), evaluated as max(x, 0) + log1p(y) with y = e^-|x| <= 1 and
+//   log1p(y) = 2 atanh(s) = 2 (s + s^3/3 + s^5/5 + ...),   s = y / (2 + y) <= 1/3,
+// whose series, cut after s^13, is accurate to ~1e-8 relative over the whole range of y, so the
+// result keeps the relative accuracy of e^-|x| (a few 1e-7) without a library log1p.
+__device__ __forceinline__ float softplus_f(float x) {
+  const float y = __expf(-fabsf(x));
+  const float s = __fdividef(y, 2.f + y);
+  const float s2 = s * s;
+  float p = fmaf(s2, 1.f / 13.f, 1.f / 11.f);
+  p = fmaf(s2, p, 1.f / 9.f);
+  p = fmaf(s2, p, 1.f / 7.f);
+  p = fmaf(s2, p, 1.f / 5.f);
+  p = fmaf(s2, p, 1.f / 3.f);
+  p = fmaf(s2, p, 1.f);
+  const float r = fmaxf(x, 0.f) + 2.f * s * p;
+  return x <= 20.f ? r : x;  // NaN takes the first branch and stays NaN
+}
 
-// 1 / (1 + e^-x); +-inf inputs give 0 / 1.
-__device__ __forceinline__ float sigmoid_f(float x) { return 1.f / (1.f + __expf(-x)); }
+// 1 / (1 + e^-x); +-inf inputs give 0 / 1 (the fast division returns 0 for denominators past
+// 2^126, the correctly rounded value to within its error bound).
+__device__ __forceinline__ float sigmoid_f(float x) { return __fdividef(1.f, 1.f + __expf(-x)); }
+
+// x * sigmoid(x) (SiLU); -inf gives NaN as -inf * 0 does.
+__device__ __forceinline__ float silu_f(float x) { return __fdividef(x, 1.f + __expf(-x)); }
 
 // ---- dtype dispatch helpers -----------------------------------------------------------------
 

@@ -48,8 +48,9 @@ struct BwdArgs {
   int clusters;     // clusters per slice = tiles / cluster size
 };
 
-// Segments per channel (time-parallel lanes) the launchers pick for a call.
-int fwd_segments(int64_t rows);
+// States per recurrence lane of the forward (1 or 2) and segments per channel of the backward
+// that the launchers pick for a call.
+int fwd_states_per_lane(int64_t rows);
 // Read and clear the device fault word of the forward / backward kernels (synchronous).
 cudaError_t read_fault_fwd(int* out);
 cudaError_t read_fault_bwd(int* out);
