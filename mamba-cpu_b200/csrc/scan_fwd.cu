@@ -111,7 +111,7 @@ __device__ __forceinline__ void recur_chunk(FwdSmem<NS>& sm, int cl, int p, cons
                                             float2 (&P)[NS], float2& sd, int lim) {
   GroupOps<NS> cur;
   group_ops<NS, WRITE_OUT, MASKED>(sm, cl, p, 0, A2, lim, sd, cur);
-#pragma unroll
+#pragma unroll 4
   for (int q = 0; q < kQuads; ++q) {
     GroupOps<NS> nxt;
     if (q + 1 < kQuads) group_ops<NS, WRITE_OUT, MASKED>(sm, cl, p, q + 1, A2, lim, sd, nxt);
