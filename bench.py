@@ -13,7 +13,8 @@ CUDA events on the launching stream (max over ranks); the step's kernels are rep
 graphs so host launch latency is not measured.
 
 `e2e` runs the public API (selective_scan_fn + autograd) with the step's inputs copied from pinned
-host memory and every output and gradient copied back, all inside the timed region.
+host memory and every output and gradient copied back, all inside the timed region; consecutive
+steps are pipelined (copies of neighbouring steps overlap the current step's kernels).
 
 `--impl reference` times the reference's own CPU kernel (mamba-cpu csrc/selective_scan.cpp built
 into oracle/_ref) with the reference's Python-side steps (B/C transpose to (b, g, l, n), zeroed
@@ -254,37 +255,77 @@ def run_ours(args):
             print(json.dumps({"ms_fwd": ms_fwd, "ms_bwd": ms_bwd, "ms_per_step": ms_step,
                               "value": E * world / (ms_step * 1e-3), "note": "--no-e2e run (profiling)"}))
         return
+    # Steps are pipelined the way an input pipeline feeds a training loop: step i + 1's inputs
+    # are copied host -> device on one stream and step i - 1's results device -> host on another
+    # while step i runs on the compute stream, with two device input buffers. Every step still
+    # moves all of its inputs and results across PCIe inside the timed region.
     pinned = {k: (None if v is None else v.pin_memory()) for k, v in host.items()}
-    outs_host = {}
     names_in = ["u", "delta", "A", "B", "C", "D", "z", "delta_bias"]
+    nbuf = 2
+    comp = torch.cuda.current_stream(dev)
+    h2d_stream, d2h_stream = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+    dbufs = [{k: (None if v is None else torch.empty(v.shape, dtype=v.dtype, device=dev))
+              for k, v in pinned.items()} for _ in range(nbuf)]
+    in_ready = [torch.cuda.Event() for _ in range(nbuf)]
+    in_free = [torch.cuda.Event() for _ in range(nbuf)]
+    out_ready = [torch.cuda.Event() for _ in range(nbuf)]
+    for ev in in_free:
+        ev.record(comp)
+    outs_host = [[] for _ in range(nbuf)]
 
-    def e2e_step():
-        dv = {k: (None if v is None else v.to(dev, non_blocking=True)) for k, v in pinned.items()}
-        leaves = {k: (None if dv[k] is None else dv[k].requires_grad_()) for k in names_in}
+    def issue_h2d(i):
+        b = i % nbuf
+        h2d_stream.wait_event(in_free[b])
+        with torch.cuda.stream(h2d_stream):
+            for k, v in pinned.items():
+                if v is not None:
+                    dbufs[b][k].copy_(v, non_blocking=True)
+        in_ready[b].record(h2d_stream)
+
+    def compute(i):
+        b = i % nbuf
+        comp.wait_event(in_ready[b])
+        dv = dbufs[b]
+        leaves = {k: (None if dv[k] is None else dv[k].detach().requires_grad_()) for k in names_in}
         with parallel.channel_sharded(group):
             out = mb.selective_scan_fn(**leaves, delta_softplus=True)
         out.backward(dv["dout"])
         res = [out.detach()] + [leaves[k].grad for k in names_in if leaves[k] is not None]
-        if not outs_host:
-            for i, r in enumerate(res):
-                outs_host[i] = torch.empty(r.shape, dtype=r.dtype, pin_memory=True)
-        for i, r in enumerate(res):
-            outs_host[i].copy_(r, non_blocking=True)
+        in_free[b].record(comp)
+        out_ready[b].record(comp)
+        return res
+
+    def issue_d2h(i, res):
+        b = i % nbuf
+        if not outs_host[b]:
+            outs_host[b] = [torch.empty(r.shape, dtype=r.dtype, pin_memory=True) for r in res]
+        d2h_stream.wait_event(out_ready[b])
+        with torch.cuda.stream(d2h_stream):
+            for hbuf, r in zip(outs_host[b], res):
+                hbuf.copy_(r, non_blocking=True)
+                r.record_stream(d2h_stream)
+
+    def run_pipeline(n):
+        issue_h2d(0)
+        for i in range(n):
+            if i + 1 < n:
+                issue_h2d(i + 1)
+            issue_d2h(i, compute(i))
+        comp.wait_stream(d2h_stream)
 
     h2d = sum(v.numel() * v.element_size() for v in pinned.values() if v is not None)
-    for _ in range(max(args.warmup, 3)):
-        e2e_step()
+    run_pipeline(max(args.warmup, 3))
     torch.cuda.synchronize(dev)
-    d2h = sum(v.numel() * v.element_size() for v in outs_host.values())
+    d2h = sum(v.numel() * v.element_size() for v in outs_host[0])
     e2e_steps = max(3, min(args.steps, 10))
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if group is not None:
         dist.barrier()
     torch.cuda.synchronize(dev)
-    e0.record()
-    for _ in range(e2e_steps):
-        e2e_step()
-    e1.record()
+    e0.record(comp)
+    h2d_stream.wait_event(e0)
+    run_pipeline(e2e_steps)
+    e1.record(comp)
     torch.cuda.synchronize(dev)
     e2e_ms = torch.tensor([e0.elapsed_time(e1) / e2e_steps], dtype=torch.float64, device=dev)
     if group is not None:

@@ -6,7 +6,7 @@ libmamba_b200.so on CUDA tensors. Non-CUDA tensors are rejected, as the referenc
 non-CPU ones.
 """
 
-from mamba_cpu_b200 import parallel
+from mamba_cpu_b200 import hf, parallel
 from mamba_cpu_b200.ops import (
     causal_conv1d_fn,
     causal_conv1d_update,
@@ -19,6 +19,7 @@ __version__ = "0.1.0"
 __all__ = [
     "causal_conv1d_fn",
     "causal_conv1d_update",
+    "hf",
     "parallel",
     "selective_scan_fn",
     "selective_state_update",

@@ -1,0 +1,169 @@
+"""Hugging Face route: run transformers' Mamba-family mixers on the B200 kernels.
+
+mamba-cpu's ``hf.patch_transformers`` (src/mamba_cpu/hf.py:63-102) wraps module-level functions
+(``mamba_selective_scan``, ...) that transformers 5.x no longer has. In transformers 5.5 each
+mixer resolves its fast path when it is constructed: ``MambaMixer.__init__`` calls
+``lazy_load_kernel("causal-conv1d")`` and ``lazy_load_kernel("mamba-ssm")``
+(transformers/models/mamba/modeling_mamba.py), and ``lazy_load_kernel`` returns whatever module is
+already registered under that name in ``transformers.integrations.hub_kernels._KERNEL_MODULE_MAPPING``.
+The mixer then takes ``cuda_kernels_forward`` when all five of ``causal_conv1d_fn``,
+``causal_conv1d_update``, ``selective_state_update``, ``selective_scan_fn`` and
+``mamba_inner_fn`` are set and its weights are on a CUDA device; CPU models keep their
+sequential PyTorch path.
+
+:func:`patch_transformers` registers modules exposing this package's functions under those names
+(and sets the globals of already-imported modeling modules, for mixers built earlier). Training
+without a cache calls ``mamba_inner_fn``; here it is composed from the package's own ops (conv1d
+with SiLU, the x / dt projections in PyTorch, the selective scan, the output projection), with
+autograd through all of them.
+"""
+
+import importlib
+import types
+from typing import Optional
+
+import torch
+import torch.nn.functional as F
+
+from .ops import causal_conv1d_fn, causal_conv1d_update, selective_scan_fn, selective_state_update
+
+_KEYS = ("causal-conv1d", "mamba-ssm", "falcon_mamba-ssm")
+_MODELS = ("mamba", "falcon_mamba", "jamba")
+_GLOBALS = ("causal_conv1d_fn", "causal_conv1d_update", "selective_state_update", "selective_scan_fn",
+            "mamba_inner_fn", "falcon_mamba_inner_fn")
+_saved: Optional[dict] = None
+
+
+def _rms_norm(x: torch.Tensor, weight: Optional[torch.Tensor], eps: float) -> torch.Tensor:
+    """x / rms(x) over the last dim, times weight (in fp32, returned in x's dtype)."""
+    xf = x.float()
+    y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
+    if weight is not None:
+        y = y * weight.float()
+    return y.to(x.dtype)
+
+
+def mamba_inner_fn(xz, conv1d_weight, conv1d_bias, x_proj_weight, delta_proj_weight, out_proj_weight,
+                   out_proj_bias, A, B=None, C=None, D=None, delta_bias=None, B_proj_bias=None,
+                   C_proj_bias=None, delta_softplus=True, checkpoint_lvl=1, b_rms_weight=None,
+                   c_rms_weight=None, dt_rms_weight=None, b_c_dt_rms_eps=1e-6):
+    """The Mamba-1 mixer body (mamba_ssm's ``mamba_inner_fn`` signature) on this package's ops.
+
+    xz: (batch, 2 * d_inner, seqlen), the in_proj output; returns (batch, seqlen, d_model).
+    ``checkpoint_lvl`` is accepted for signature compatibility (nothing is recomputed here beyond
+    what the scan op's backward does itself). The optional RMS weights are falcon-mamba's
+    normalisations of dt, B and C.
+    """
+    batch, _, seqlen = xz.shape
+    d_state = A.shape[-1]
+    dt_rank = delta_proj_weight.shape[1]
+    x, z = xz.chunk(2, dim=1)
+    x = causal_conv1d_fn(x, conv1d_weight.reshape(conv1d_weight.shape[0], -1), conv1d_bias, activation="silu")
+    d_inner = x.shape[1]
+    x_dbl = F.linear(x.transpose(1, 2).reshape(batch * seqlen, d_inner), x_proj_weight)  # (b l, r + 2n)
+    dt = x_dbl[:, :dt_rank]
+    if dt_rms_weight is not None:
+        dt = _rms_norm(dt, dt_rms_weight, b_c_dt_rms_eps)
+    delta = (delta_proj_weight @ dt.t()).reshape(d_inner, batch, seqlen).transpose(0, 1)  # (b, d, l)
+
+    def _bc(M, start, bias, rms_w):
+        if M is not None:
+            return M
+        M = x_dbl[:, start:start + d_state]
+        if bias is not None:
+            M = M + bias.to(M.dtype)
+        if rms_w is not None:
+            M = _rms_norm(M, rms_w, b_c_dt_rms_eps)
+        return M.reshape(batch, seqlen, d_state).transpose(1, 2)  # (b, n, l)
+
+    B = _bc(B, dt_rank, B_proj_bias, b_rms_weight)
+    C = _bc(C, dt_rank + d_state, C_proj_bias, c_rms_weight)
+    y = selective_scan_fn(x, delta, A, B, C, D, z, delta_bias, delta_softplus)
+    return F.linear(y.transpose(1, 2), out_proj_weight, out_proj_bias)
+
+
+def _values() -> dict:
+    return {
+        "causal_conv1d_fn": causal_conv1d_fn,
+        "causal_conv1d_update": causal_conv1d_update,
+        "selective_state_update": selective_state_update,
+        "selective_scan_fn": selective_scan_fn,
+        "mamba_inner_fn": mamba_inner_fn,
+        "falcon_mamba_inner_fn": mamba_inner_fn,
+    }
+
+
+def kernel_modules() -> dict:
+    """The modules registered under transformers' kernel names."""
+    v = _values()
+    conv = types.ModuleType("mamba_cpu_b200.hf.causal_conv1d")
+    conv.causal_conv1d_fn = v["causal_conv1d_fn"]
+    conv.causal_conv1d_update = v["causal_conv1d_update"]
+    ssm = types.ModuleType("mamba_cpu_b200.hf.mamba_ssm")
+    for name in ("selective_scan_fn", "selective_state_update", "mamba_inner_fn", "falcon_mamba_inner_fn"):
+        setattr(ssm, name, v[name])
+    return {"causal-conv1d": conv, "mamba-ssm": ssm, "falcon_mamba-ssm": ssm}
+
+
+def patch_transformers() -> list:
+    """Route transformers' Mamba / FalconMamba / Jamba mixers with CUDA weights to this package.
+
+    Call before building the model (mixers resolve their kernels in ``__init__``); modeling
+    modules already imported also get their globals set, so earlier mixers switch too. Returns
+    the names of the modeling modules that were patched. Idempotent; undone by
+    :func:`unpatch_transformers`.
+    """
+    global _saved
+    from transformers.integrations import hub_kernels
+
+    mapping = hub_kernels._KERNEL_MODULE_MAPPING
+    if _saved is None:
+        _saved = {"mapping": {k: mapping.get(k, _MISSING) for k in _KEYS}, "globals": {}}
+    mapping.update(kernel_modules())
+    patched = []
+    values = _values()
+    for model in _MODELS:
+        try:
+            mod = importlib.import_module(f"transformers.models.{model}.modeling_{model}")
+        except ImportError:
+            continue
+        for name in _GLOBALS:
+            if name == "falcon_mamba_inner_fn" and model != "falcon_mamba":
+                continue
+            if name == "mamba_inner_fn" and model == "falcon_mamba":
+                continue
+            _saved["globals"].setdefault((mod.__name__, name), getattr(mod, name, _MISSING))
+            setattr(mod, name, values[name])
+        patched.append(mod.__name__)
+    return patched
+
+
+def unpatch_transformers() -> None:
+    """Restore transformers' kernel mapping and modeling globals to their state before patching."""
+    global _saved
+    if _saved is None:
+        return
+    from transformers.integrations import hub_kernels
+
+    mapping = hub_kernels._KERNEL_MODULE_MAPPING
+    for k, v in _saved["mapping"].items():
+        if v is _MISSING:
+            mapping.pop(k, None)
+        else:
+            mapping[k] = v
+    for (modname, name), v in _saved["globals"].items():
+        mod = importlib.import_module(modname)
+        if v is _MISSING:
+            if hasattr(mod, name):
+                delattr(mod, name)
+        else:
+            setattr(mod, name, v)
+    _saved = None
+
+
+class _Missing:
+    def __repr__(self):
+        return "<missing>"
+
+
+_MISSING = _Missing()

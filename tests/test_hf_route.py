@@ -1,0 +1,137 @@
+"""Hugging Face route (transformers 5.5): MambaForCausalLM mixers on the B200 kernels.
+
+CPU tests check the registration (the kernel-name mapping transformers consults when a mixer is
+built, the modeling-module globals, and undoing both). GPU tests run a small random-init
+MambaForCausalLM on CUDA through the patched fast path -- prefill (selective_scan_fn +
+causal_conv1d_fn), training (mamba_inner_fn, with gradients) and cached decoding
+(causal_conv1d_update + selective_state_update) -- against the same model on transformers' own
+sequential PyTorch path.
+"""
+
+import contextlib
+
+import pytest
+import torch
+
+transformers = pytest.importorskip("transformers")
+
+from mamba_cpu_b200 import hf  # noqa: E402
+
+from helpers import assert_close  # noqa: E402
+
+FAST = ("causal_conv1d_fn", "causal_conv1d_update", "selective_state_update", "selective_scan_fn", "mamba_inner_fn")
+
+
+def _config():
+    from transformers import MambaConfig
+
+    return MambaConfig(vocab_size=96, hidden_size=64, state_size=16, num_hidden_layers=2, expand=2, conv_kernel=4,
+                       time_step_rank=8, use_mambapy=False)
+
+
+@contextlib.contextmanager
+def _patched():
+    hf.patch_transformers()
+    try:
+        yield
+    finally:
+        hf.unpatch_transformers()
+
+
+@contextlib.contextmanager
+def _slow_path():
+    """transformers' sequential PyTorch mixer: every fast-path function unset."""
+    from transformers.models.mamba import modeling_mamba as mm
+
+    saved = {n: getattr(mm, n, None) for n in FAST}
+    for n in FAST:
+        setattr(mm, n, None)
+    try:
+        yield
+    finally:
+        for n, v in saved.items():
+            setattr(mm, n, v)
+
+
+def test_patch_registers_modules_and_globals():
+    from transformers.integrations import hub_kernels
+    from transformers.models.mamba import modeling_mamba as mm
+
+    before = dict(hub_kernels._KERNEL_MODULE_MAPPING)
+    with _patched():
+        mapping = hub_kernels._KERNEL_MODULE_MAPPING
+        assert mapping["causal-conv1d"].causal_conv1d_fn is hf.causal_conv1d_fn
+        assert mapping["causal-conv1d"].causal_conv1d_update is hf.causal_conv1d_update
+        for n in ("selective_scan_fn", "selective_state_update", "mamba_inner_fn"):
+            assert getattr(mapping["mamba-ssm"], n) is getattr(hf, n)
+        # a mixer built now resolves the package's functions through lazy_load_kernel
+        from transformers import MambaModel
+
+        MambaModel(_config())
+        for n in FAST:
+            assert getattr(mm, n) is getattr(hf, n), n
+    assert dict(hub_kernels._KERNEL_MODULE_MAPPING) == before
+
+
+def test_mamba_inner_fn_signature_matches_mamba_ssm():
+    import inspect
+
+    params = list(inspect.signature(hf.mamba_inner_fn).parameters)
+    assert params[:11] == ["xz", "conv1d_weight", "conv1d_bias", "x_proj_weight", "delta_proj_weight",
+                           "out_proj_weight", "out_proj_bias", "A", "B", "C", "D"]
+    for kw in ("delta_bias", "delta_softplus", "b_rms_weight", "c_rms_weight", "dt_rms_weight", "b_c_dt_rms_eps"):
+        assert kw in params
+
+
+def _model():
+    from transformers import MambaForCausalLM
+
+    torch.manual_seed(0)
+    with _patched():
+        model = MambaForCausalLM(_config())
+    return model.cuda().float()
+
+
+@pytest.mark.gpu
+def test_prefill_matches_sequential_path():
+    model = _model().eval()
+    ids = torch.randint(0, 96, (2, 150), generator=torch.Generator().manual_seed(1)).cuda()
+    with torch.no_grad(), _patched():
+        fast = model(ids).logits
+    with torch.no_grad(), _slow_path():
+        ref = model(ids).logits
+    assert_close(fast, ref, 1e-4, 1e-4, "logits")
+
+
+@pytest.mark.gpu
+def test_training_step_matches_sequential_path():
+    model = _model().train()
+    ids = torch.randint(0, 96, (2, 100), generator=torch.Generator().manual_seed(2)).cuda()
+    with _patched():
+        loss = model(ids, labels=ids).loss
+        loss.backward()
+    fast = {n: p.grad.detach().clone() for n, p in model.named_parameters() if p.grad is not None}
+    fast_loss = loss.item()
+    model.zero_grad(set_to_none=True)
+    with _slow_path():
+        loss = model(ids, labels=ids).loss
+        loss.backward()
+    assert abs(fast_loss - loss.item()) <= 1e-5 * abs(loss.item())
+    assert len(fast) == sum(1 for _ in model.parameters())
+    for n, p in model.named_parameters():
+        scale = max(1e-6, float(p.grad.abs().max()))
+        assert_close(fast[n] / scale, p.grad / scale, 1e-3, 1e-4, n)
+
+
+@pytest.mark.gpu
+def test_cached_decoding_matches_sequential_path():
+    model = _model().eval()
+    ids = torch.randint(0, 96, (2, 12), generator=torch.Generator().manual_seed(3)).cuda()
+    kw = dict(max_new_tokens=6, do_sample=False, return_dict_in_generate=True, output_scores=True)
+    with torch.no_grad(), _patched():
+        fast = model.generate(ids, **kw)
+    with torch.no_grad(), _slow_path():
+        ref = model.generate(ids, **kw)
+    assert torch.equal(fast.sequences, ref.sequences)
+    for a, b in zip(fast.scores, ref.scores):
+        assert_close(a, b, 1e-4, 1e-4, "scores")
