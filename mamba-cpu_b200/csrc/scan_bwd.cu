@@ -31,6 +31,7 @@
 #include "scan.cuh"
 #include "segscan.cuh"
 #include "stage.cuh"
+#include "tmem.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -43,17 +44,20 @@ constexpr int kRedFloats = kMaxState * 2 * kChunk;  // one CTA's dB|dC chunk par
 
 constexpr int ilog2(int v) { return v <= 1 ? 0 : 1 + ilog2(v / 2); }
 
-constexpr int kGroup = 4;  // states whose warp partials are summed together (one block barrier)
+// TMEM columns per CTA: per thread, the adjoint gh entering the current chunk (columns 0..15)
+// and the dA partial of each state (16..31).
+constexpr uint32_t kTmemCols = 32;
+constexpr int kColDA = kMaxState;
 
 template <typename TW, int CPC>
 struct BwdSmem {
   TW bc[2][2][kMaxState][TileRow<TW>::kStride];   // [buf][B|C][n][staged t]
   float hst[2][CPC][kMaxState];                   // [buf][channel][n]: state at the chunk start
-  float red[2][kBwdWarps][kGroup * 2 * kChunk];   // [group parity][warp]: dB|dC partials of a state group
+  float red[kBwdWarps][kRedFloats];               // [warp]: dB|dC partials of the chunk
   float red_out[2][kRedFloats];                   // CTA sums of a chunk, double-buffered for cluster readers
-  float car[2][kMaxState][kBwdWarps * 32];        // [gh | dA partial][n][thread]
   float A[CPC][kMaxState];
   uint64_t bar[2];
+  uint32_t tmem_base;
 };
 
 template <typename TI, typename TW, int S, bool HAS_Z, bool STAGED, bool MASKED>
@@ -62,7 +66,7 @@ __device__ __forceinline__ void bwd_chunk(const BwdArgs& a, BwdSmem<TW, kBwdWarp
                                           int lane, int warp, int c, int s, const TW* Bbase, const TW* Cbase,
                                           float Dv, float bias, const TI* urow, const TI* drow, const TI* dorow,
                                           const TI* zrow, float& dDacc, float& dbacc, int& rbuf,
-                                          cg::cluster_group& cluster) {
+                                          uint32_t tcar, cg::cluster_group& cluster) {
   constexpr int K = kChunk / S;
   constexpr int CW = 32 / S;
   constexpr int R = ilog2(CW);
@@ -104,148 +108,231 @@ __device__ __forceinline__ void bwd_chunk(const BwdArgs& a, BwdSmem<TW, kBwdWarp
   const TW* tB = &sm.bc[buf][0][0][0];
   const TW* tC = &sm.bc[buf][1][0][0];
 
+  // States are processed in pairs (n0, n0 + 1): the two states' dependency chains (local maps,
+  // shuffle scans, the h and adjoint recurrences) are independent and interleave, which hides
+  // their latencies; the per-step products that do not sit on a chain run as f32x2 pairs of
+  // timesteps. An odd dstate pads the last pair with an inert state (A = B = C = 0).
   const int total4 = N * 2 * kChunk / 4;
-  int gpar = 0;
 #pragma unroll 1
-  for (int ng = 0; ng < N; ng += kGroup, gpar ^= 1) {
-    const int nend = min(ng + kGroup, N);
-#pragma unroll 1
-  for (int n = ng; n < nend; ++n) {
-    const float An = sm.A[cl_c][n];
-    const float A2n = An * kLog2e;
-    // Invalid (padding) lanes must stay finite: they contribute dy = 0 to the dB/dC sums, and
-    // 0 * NaN from an unwritten restart-state slot would poison them.
-    float hck = 0.f;
-    if (k > 0 && valid) {
-      if constexpr (STAGED)
-        hck = sm.hst[buf][cl_c][n];
-      else
-        hck = a.states[(row * f.nchunks + (k - 1)) * N + n];
-    }
-    float Bn[K], Cn[K], av[K], hs[K], bv[K];
-    if constexpr (STAGED) {
-      constexpr int kRS = TileRow<TW>::kStride;
-      const int tpos = TileRow<TW>::pos(s * K);
-      load_cached_smem<TW, K>(tB + n * kRS + tpos, Bn);
-      load_cached_smem<TW, K>(tC + n * kRS + tpos, Cn);
-    } else {
-      load_bc_items<TW, K>(Bbase + n * f.sBn, f.sBl, t0, L, MASKED ? false : (f.vec_bc != 0), Bn);
-      load_bc_items<TW, K>(Cbase + n * f.sCn, f.sCl, t0, L, MASKED ? false : (f.vec_bc != 0), Cn);
-    }
+  for (int n0 = 0; n0 < N; n0 += 2) {
+    // this thread's carries of the pair (TMEM): gh entering the chunk, dA partial
+    float gcn[2], dAc[2];
+    tmem_wait_st();  // the previous pair's carry stores have landed
+    tmem_ld2(tcar + n0, gcn[0], gcn[1]);
+    tmem_ld2(tcar + kColDA + n0, dAc[0], dAc[1]);
+    float An[2], A2n[2], hck[2];
+    float Bn[2][K], Cn[2][K], av[2][K], bv[2][K], hs[2][K], gg[2][K];
 #pragma unroll
-    for (int i = 0; i < K; ++i) {
-      av[i] = ex2(dt[i] * A2n);
-      bv[i] = dtu[i] * Bn[i];
-    }
-    if (MASKED) {
+    for (int j = 0; j < 2; ++j) {
+      const int n = n0 + j;
+      const bool live = n < N;
+      An[j] = live ? sm.A[cl_c][n] : 0.f;
+      A2n[j] = An[j] * kLog2e;
+      // Invalid (padding) lanes must stay finite: they contribute dy = 0 to the dB/dC sums, and
+      // 0 * NaN from an unwritten restart-state slot would poison them.
+      hck[j] = 0.f;
+      if (k > 0 && valid && live) {
+        if constexpr (STAGED)
+          hck[j] = sm.hst[buf][cl_c][n];
+        else
+          hck[j] = a.states[(row * f.nchunks + (k - 1)) * N + n];
+      }
+      if (!live) {
 #pragma unroll
-      for (int i = 0; i < K; ++i)
-        if (t0 + i >= L) av[i] = 1.f;
+        for (int i = 0; i < K; ++i) Bn[j][i] = Cn[j][i] = 0.f;
+      } else if constexpr (STAGED) {
+        constexpr int kRS = TileRow<TW>::kStride;
+        const int tpos = TileRow<TW>::pos(s * K);
+        load_cached_smem<TW, K>(tB + n * kRS + tpos, Bn[j]);
+        load_cached_smem<TW, K>(tC + n * kRS + tpos, Cn[j]);
+      } else {
+        load_bc_items<TW, K>(Bbase + n * f.sBn, f.sBl, t0, L, MASKED ? false : (f.vec_bc != 0), Bn[j]);
+        load_bc_items<TW, K>(Cbase + n * f.sCn, f.sCl, t0, L, MASKED ? false : (f.vec_bc != 0), Cn[j]);
+      }
+      const float2 a2 = make_float2(A2n[j], A2n[j]);
+#pragma unroll
+      for (int i = 0; i < K; i += 2) {
+        const float2 x = __fmul2_rn(make_float2(dt[i], dt[i + 1]), a2);
+        av[j][i] = ex2(x.x);
+        av[j][i + 1] = ex2(x.y);
+        const float2 b = __fmul2_rn(make_float2(dtu[i], dtu[i + 1]), make_float2(Bn[j][i], Bn[j][i + 1]));
+        bv[j][i] = b.x;
+        bv[j][i + 1] = b.y;
+      }
+      if (MASKED) {
+#pragma unroll
+        for (int i = 0; i < K; ++i)
+          if (t0 + i >= L) av[j][i] = 1.f;
+      }
     }
     // -- forward: rebuild h inside the chunk
-    const float Aloc = seg_decay(An, sdt);  // this segment's total decay
-    float h0;
-    if constexpr (S > 1) {
-      float Al = Aloc, Bl = bv[0];
+    float Aloc[2], h0[2];
 #pragma unroll
-      for (int i = 1; i < K; ++i) Bl = fmaf(av[i], Bl, bv[i]);
-      scan_up<S>(s, Al, Bl);
-      float Ae = __shfl_up_sync(kFull, Al, 1, S);
-      float Be = __shfl_up_sync(kFull, Bl, 1, S);
-      if (s == 0) {
-        Ae = 1.f;
-        Be = 0.f;
+    for (int j = 0; j < 2; ++j) Aloc[j] = seg_decay(An[j], sdt);  // the segment's total decay
+    if constexpr (S > 1) {
+      float Al[2], Bl[2];
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        Al[j] = Aloc[j];
+        Bl[j] = bv[j][0];
       }
-      h0 = fmaf(Ae, hck, Be);
+#pragma unroll
+      for (int i = 1; i < K; ++i) {
+#pragma unroll
+        for (int j = 0; j < 2; ++j) Bl[j] = fmaf(av[j][i], Bl[j], bv[j][i]);
+      }
+      scan_up2<S>(s, Al, Bl);
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        float Ae = __shfl_up_sync(kFull, Al[j], 1, S);
+        float Be = __shfl_up_sync(kFull, Bl[j], 1, S);
+        if (s == 0) {
+          Ae = 1.f;
+          Be = 0.f;
+        }
+        h0[j] = fmaf(Ae, hck[j], Be);
+      }
     } else {
-      h0 = hck;
+      h0[0] = hck[0];
+      h0[1] = hck[1];
     }
     {
-      float h = h0;
+      float h[2] = {h0[0], h0[1]};
 #pragma unroll
       for (int i = 0; i < K; ++i) {
-        h = fmaf(av[i], h, bv[i]);
-        hs[i] = h;
-        if constexpr (HAS_Z) y[i] = fmaf(h, Cn[i], y[i]);
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          h[j] = fmaf(av[j][i], h[j], bv[j][i]);
+          hs[j][i] = h[j];
+        }
+      }
+    }
+    if constexpr (HAS_Z) {
+#pragma unroll
+      for (int i = 0; i < K; i += 2) {
+        float2 yy = make_float2(y[i], y[i + 1]);
+#pragma unroll
+        for (int j = 0; j < 2; ++j)
+          yy = __ffma2_rn(make_float2(hs[j][i], hs[j][i + 1]), make_float2(Cn[j][i], Cn[j][i + 1]), yy);
+        y[i] = yy.x;
+        y[i + 1] = yy.y;
       }
     }
     // -- reverse: gh entering this lane's segment from later timesteps
-    const int tid = threadIdx.x;
-    const float gcn = sm.car[0][n][tid];
-    float gh, Ar = 1.f, Gr = 0.f;
+    float gh[2], Ar[2] = {1.f, 1.f}, Gr[2] = {0.f, 0.f};
+    tmem_wait_ld();
     if constexpr (S > 1) {
-      float Gl = 0.f;
+      float Gl[2] = {0.f, 0.f};
 #pragma unroll
-      for (int i = K - 1; i >= 0; --i) Gl = av[i] * fmaf(dy[i], Cn[i], Gl);
-      Ar = Aloc;
-      Gr = Gl;
-      scan_down<S>(s, Ar, Gr);
-      float Ae = __shfl_down_sync(kFull, Ar, 1, S);
-      float Ge = __shfl_down_sync(kFull, Gr, 1, S);
-      if (s == S - 1) {
-        Ae = 1.f;
-        Ge = 0.f;
+      for (int i = K - 1; i >= 0; --i) {
+#pragma unroll
+        for (int j = 0; j < 2; ++j) Gl[j] = av[j][i] * fmaf(dy[i], Cn[j][i], Gl[j]);
       }
-      gh = fmaf(Ae, gcn, Ge);
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        Ar[j] = Aloc[j];
+        Gr[j] = Gl[j];
+      }
+      scan_down2<S>(s, Ar, Gr);
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        float Ae = __shfl_down_sync(kFull, Ar[j], 1, S);
+        float Ge = __shfl_down_sync(kFull, Gr[j], 1, S);
+        if (s == S - 1) {
+          Ae = 1.f;
+          Ge = 0.f;
+        }
+        gh[j] = fmaf(Ae, gcn[j], Ge);
+      }
     } else {
-      gh = gcn;
+      gh[0] = gcn[0];
+      gh[1] = gcn[1];
     }
-    float dAn = sm.car[1][n][tid];
-    float v[2 * K];  // [dB items | dC items] of this lane's channel
+    // adjoint chain: G_t = gh_t + dy_t C_t, gh_{t-1} = a_t G_t
 #pragma unroll
     for (int i = K - 1; i >= 0; --i) {
-      const float gg = fmaf(dy[i], Cn[i], gh);
-      v[K + i] = dy[i] * hs[i];
-      const float hp = i > 0 ? hs[i - 1] : h0;
-      const float xx = gg * (av[i] * hp);
-      dAn = fmaf(xx, dt[i], dAn);
-      xA[i] = fmaf(xx, An, xA[i]);
-      gB[i] = fmaf(gg, Bn[i], gB[i]);
-      v[i] = gg * dtu[i];
-      gh = gg * av[i];
-    }
-    // gh entering the previous chunk: the scanned map of the whole chunk applied to gcn
-    if constexpr (S > 1)
-      gh = __shfl_sync(kFull, fmaf(Ar, gcn, Gr), 0, S);
-    sm.car[0][n][tid] = gh;
-    sm.car[1][n][tid] = dAn;
-    // -- reduce-scatter dB|dC over the CW channel lanes holding the same timesteps
-    int io = 0;
 #pragma unroll
-    for (int r = 0; r < R; ++r) {
-      const int mask = S << r;
-      const bool upper = (lane & mask) != 0;
-      const int half = K >> r;
-#pragma unroll
-      for (int j = 0; j < half; ++j) {
-        const float send = upper ? v[j] : v[half + j];
-        const float keep = upper ? v[half + j] : v[j];
-        v[j] = keep + __shfl_xor_sync(kFull, send, mask);
+      for (int j = 0; j < 2; ++j) {
+        gg[j][i] = fmaf(dy[i], Cn[j][i], gh[j]);
+        gh[j] = gg[j][i] * av[j][i];
       }
-      if (r > 0 && upper) io += half;
     }
-    const int q = (lane & S) ? 1 : 0;
-    *reinterpret_cast<float4*>(&sm.red[gpar][warp][((n - ng) * 2 + q) * kChunk + s * K + io]) =
-        make_float4(v[0], v[1], v[2], v[3]);
-  }
-    // -- sum the group's partials over the warps of the CTA (red is double-buffered by group
-    //    parity, so one barrier per group suffices)
-    __syncthreads();
+    // carries into the previous chunk: gh entering it (the scanned map of the whole chunk
+    // applied to gcn) and this lane's dA partial
     {
-      float4* ro = reinterpret_cast<float4*>(sm.red_out[rbuf]) + ng * 2 * kChunk / 4;
-      const int g4 = (nend - ng) * 2 * kChunk / 4;
-      for (int f4 = threadIdx.x; f4 < g4; f4 += blockDim.x) {
-        float4 acc = reinterpret_cast<const float4*>(sm.red[gpar][0])[f4];
+      float ghc[2] = {gh[0], gh[1]};
+      if constexpr (S > 1) {
 #pragma unroll
-        for (int w = 1; w < kBwdWarps; ++w) {
-          const float4 o = reinterpret_cast<const float4*>(sm.red[gpar][w])[f4];
-          acc.x += o.x;
-          acc.y += o.y;
-          acc.z += o.z;
-          acc.w += o.w;
-        }
-        ro[f4] = acc;
+        for (int j = 0; j < 2; ++j) ghc[j] = __shfl_sync(kFull, fmaf(Ar[j], gcn[j], Gr[j]), 0, S);
       }
+      tmem_st2(tcar + n0, ghc[0], ghc[1]);
+    }
+    // -- per state: the gradient terms of the K steps (f32x2 over timestep pairs), then the
+    //    reduce-scatter of dB|dC over the CW channel lanes holding the same timesteps
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int n = n0 + j;
+      const float2 an2 = make_float2(An[j], An[j]);
+      float2 dA2 = make_float2(0.f, 0.f);
+      float v[2 * K];  // [dB items | dC items] of this lane's channel
+#pragma unroll
+      for (int i = 0; i < K; i += 2) {
+        const float2 g2 = make_float2(gg[j][i], gg[j][i + 1]);
+        const float2 h2 = make_float2(hs[j][i], hs[j][i + 1]);
+        // a_t h_{t-1} = h_t - b_t
+        const float2 xx = __fmul2_rn(g2, __fadd2_rn(h2, make_float2(-bv[j][i], -bv[j][i + 1])));
+        dA2 = __ffma2_rn(xx, make_float2(dt[i], dt[i + 1]), dA2);
+        const float2 xa = __ffma2_rn(xx, an2, make_float2(xA[i], xA[i + 1]));
+        xA[i] = xa.x;
+        xA[i + 1] = xa.y;
+        const float2 gb = __ffma2_rn(g2, make_float2(Bn[j][i], Bn[j][i + 1]), make_float2(gB[i], gB[i + 1]));
+        gB[i] = gb.x;
+        gB[i + 1] = gb.y;
+        const float2 vb = __fmul2_rn(g2, make_float2(dtu[i], dtu[i + 1]));
+        const float2 vc = __fmul2_rn(make_float2(dy[i], dy[i + 1]), h2);
+        v[i] = vb.x;
+        v[i + 1] = vb.y;
+        v[K + i] = vc.x;
+        v[K + i + 1] = vc.y;
+      }
+      dAc[j] += dA2.x + dA2.y;
+      int io = 0;
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const int mask = S << r;
+        const bool upper = (lane & mask) != 0;
+        const int half = K >> r;
+#pragma unroll
+        for (int q = 0; q < half; ++q) {
+          const float send = upper ? v[q] : v[half + q];
+          const float keep = upper ? v[half + q] : v[q];
+          v[q] = keep + __shfl_xor_sync(kFull, send, mask);
+        }
+        if (r > 0 && upper) io += half;
+      }
+      const int q = (lane & S) ? 1 : 0;
+      if (n < N)
+        *reinterpret_cast<float4*>(&sm.red[warp][(n * 2 + q) * kChunk + s * K + io]) =
+            make_float4(v[0], v[1], v[2], v[3]);
+    }
+    tmem_st2(tcar + kColDA + n0, dAc[0], dAc[1]);
+  }
+  // -- sum the chunk's partials over the warps of the CTA. red is rewritten only in the next
+  //    chunk, after the cluster barrier below, which every thread reaches after this sum.
+  __syncthreads();
+  {
+    float4* ro = reinterpret_cast<float4*>(sm.red_out[rbuf]);
+    for (int f4 = threadIdx.x; f4 < total4; f4 += blockDim.x) {
+      float4 acc = reinterpret_cast<const float4*>(sm.red[0])[f4];
+#pragma unroll
+      for (int w = 1; w < kBwdWarps; ++w) {
+        const float4 o = reinterpret_cast<const float4*>(sm.red[w])[f4];
+        acc.x += o.x;
+        acc.y += o.y;
+        acc.z += o.z;
+        acc.w += o.w;
+      }
+      ro[f4] = acc;
     }
   }
 
@@ -365,11 +452,8 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3) scan_bwd_kernel(const BwdAr
   const float bias = f.delta_bias ? f.delta_bias[d] : 0.f;
   const bool staged = f.vec_bc != 0;
 
-  // per-lane carries and the channels' A rows
-  for (int n = 0; n < N; ++n) {
-    sm.car[0][n][threadIdx.x] = (valid && a.dlast != nullptr) ? a.dlast[row * N + n] : 0.f;
-    sm.car[1][n][threadIdx.x] = 0.f;
-  }
+  // TMEM for the per-thread carries (warp 0 allocates; <= 4 co-resident CTAs x 32 columns)
+  if (warp == 0) tmem_alloc(&sm.tmem_base, kTmemCols);
   for (int i = threadIdx.x; i < CPC * N; i += blockDim.x) {
     const int ch = i / N, n = i % N;
     const int64_t dd = g * f.dpg + (tile_c0 + ch < f.dpg ? tile_c0 + ch : 0);
@@ -380,7 +464,21 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3) scan_bwd_kernel(const BwdAr
     mbar_init(&sm.bar[1], 1);
     mbar_fence_init();
   }
+  tmem_fence_before_sync();
   __syncthreads();
+  tmem_fence_after_sync();
+  const uint32_t tcar = tmem_lane_addr(sm.tmem_base, warp, 0);
+  {
+    // carries: gh entering the last chunk = dlast_state, dA partials = 0
+    float init[kMaxState];
+#pragma unroll
+    for (int n = 0; n < kMaxState; ++n)
+      init[n] = (valid && n < N && a.dlast != nullptr) ? a.dlast[row * N + n] : 0.f;
+    tmem_st16(tcar, init);
+#pragma unroll
+    for (int n = 0; n < kMaxState; ++n) init[n] = 0.f;
+    tmem_st16(tcar + kColDA, init);
+  }
 
   // first row (global index) of this CTA's channels, for the restart-state copies
   const int64_t row_c0 = b * f.dim + g * f.dpg + tile_c0;
@@ -422,7 +520,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3) scan_bwd_kernel(const BwdAr
   for (int k = f.nchunks - 1; k >= nfull; --k) {
     bwd_chunk<TI, TW, S, HAS_Z, false, true>(a, sm, 0, k, row, slice, cluster_idx, cl_c, valid, lane, warp, c, s,
                                              Bbase, Cbase, Dv, bias, urow, drow, dorow, zrow, dDacc, dbacc, rbuf,
-                                             cluster);
+                                             tcar, cluster);
   }
   // Full chunks, last to first: B/C + restart states staged one chunk ahead by the bulk-copy
   // engine; the lane's own rows of the next chunk are prefetched into L2.
@@ -441,17 +539,24 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3) scan_bwd_kernel(const BwdAr
     mbar_wait(&sm.bar[buf], (uint32_t)(((nfull - 1 - k) >> 1) & 1));
     bwd_chunk<TI, TW, S, HAS_Z, true, false>(a, sm, buf, k, row, slice, cluster_idx, cl_c, valid, lane, warp, c, s,
                                              Bbase, Cbase, Dv, bias, urow, drow, dorow, zrow, dDacc, dbacc, rbuf,
-                                             cluster);
+                                             tcar, cluster);
     // bwd_chunk ends with cluster.sync() after its last shared-memory read of this buffer, so the
     // next iteration may refill it.
   }
 
   // -- per-row partials of dA / dD / ddelta_bias: sum the S segment lanes of the channel
-  for (int n = 0; n < N; ++n) {
-    float v = sm.car[1][n][threadIdx.x];
+  {
+    float dAp[kMaxState];
+    tmem_wait_st();
+    tmem_ld16(tcar + kColDA, dAp);
+    tmem_wait_ld();
 #pragma unroll
-    for (int off = S / 2; off > 0; off >>= 1) v += __shfl_xor_sync(kFull, v, off, S);
-    if (valid && s == 0) a.part_A[row * N + n] = v;
+    for (int n = 0; n < kMaxState; ++n) {
+      float v = dAp[n];
+#pragma unroll
+      for (int off = S / 2; off > 0; off >>= 1) v += __shfl_xor_sync(kFull, v, off, S);
+      if (valid && s == 0 && n < N) a.part_A[row * N + n] = v;
+    }
   }
 #pragma unroll
   for (int off = S / 2; off > 0; off >>= 1) {
@@ -463,7 +568,11 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3) scan_bwd_kernel(const BwdAr
     a.part_db[row] = dbacc;
   }
   // Peers may still be reading this CTA's red_out through distributed shared memory.
+  tmem_fence_before_sync();
   cluster.sync();
+  // every thread of the CTA is done with TMEM: the allocating warp frees it
+  tmem_fence_after_sync();
+  if (warp == 0) tmem_dealloc(sm.tmem_base, kTmemCols);
 }
 
 template <typename TI, typename TW, int S>

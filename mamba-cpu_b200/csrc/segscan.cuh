@@ -52,4 +52,45 @@ __device__ __forceinline__ void scan_down(int s, float& A, float& B) {
   }
 }
 
+// scan_up / scan_down of two independent states at once (their shuffles and FMAs interleave).
+template <int S>
+__device__ __forceinline__ void scan_up2(int s, float (&A)[2], float (&B)[2]) {
+#pragma unroll
+  for (int off = 1; off < S; off <<= 1) {
+    float Ap[2], Bp[2];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      Ap[j] = __shfl_up_sync(kFullMask, A[j], off, S);
+      Bp[j] = __shfl_up_sync(kFullMask, B[j], off, S);
+    }
+    if (s >= off) {
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        B[j] = fmaf(A[j], Bp[j], B[j]);
+        A[j] *= Ap[j];
+      }
+    }
+  }
+}
+
+template <int S>
+__device__ __forceinline__ void scan_down2(int s, float (&A)[2], float (&B)[2]) {
+#pragma unroll
+  for (int off = 1; off < S; off <<= 1) {
+    float An[2], Bn[2];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      An[j] = __shfl_down_sync(kFullMask, A[j], off, S);
+      Bn[j] = __shfl_down_sync(kFullMask, B[j], off, S);
+    }
+    if (s + off < S) {
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        B[j] = fmaf(A[j], Bn[j], B[j]);
+        A[j] *= An[j];
+      }
+    }
+  }
+}
+
 }  // namespace mb200
