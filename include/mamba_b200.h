@@ -72,6 +72,9 @@ extern "C" {
  *   chunk_states     : (batch, dim, ceil(seqlen / MB200_CHUNK), dstate) float32 or NULL: the state
  *                      after every MB200_CHUNK timesteps, which the backward uses instead of
  *                      recomputing the forward from t = 0.
+ *   initial_state    : (batch, dim, dstate) float32 or NULL: the state before the first step
+ *                      (zeros when NULL, which is the reference's behaviour). Lets a sequence
+ *                      be scanned in pieces, e.g. split across GPUs.
  * io_dtype in {F32, BF16, F16}; bc_dtype is F32 or equal to io_dtype.
  */
 typedef struct mb200_scan_fwd_params {
@@ -86,6 +89,7 @@ typedef struct mb200_scan_fwd_params {
   void* out;
   float* last_state;
   float* chunk_states;
+  const float* initial_state;
   int64_t batch, dim, seqlen, dstate, ngroups;
   int64_t B_batch_stride, B_group_stride, B_dstate_stride, B_seqlen_stride;
   int64_t C_batch_stride, C_group_stride, C_dstate_stride, C_seqlen_stride;
@@ -107,6 +111,8 @@ typedef struct mb200_scan_fwd_params {
  *   dB, dC           : (batch, ngroups, dstate, seqlen) contiguous, dtype dbc_dtype (F32 or
  *                      fwd.bc_dtype); overwritten
  *   dD, ddelta_bias  : (dim) float32, summed over batch; either may be NULL to skip it
+ *   dinitial_state   : (batch, dim, dstate) float32 or NULL: gradient with respect to
+ *                      fwd.initial_state (the adjoint entering the first step)
  * The reference returns dA/dD/ddelta_bias as per-batch partials that its Python layer sums
  * (selective_scan_interface.py:87); here the sum over batch happens on the device.
  */
@@ -122,6 +128,7 @@ typedef struct mb200_scan_bwd_params {
   void* dC;
   float* dD;
   float* ddelta_bias;
+  float* dinitial_state;
   int32_t dbc_dtype;
   int32_t reserved;
 } mb200_scan_bwd_params;

@@ -47,6 +47,7 @@ int build_scan_args(const mb200_scan_fwd_params* p, bool need_out, ScanArgs* a) 
   a->out = p->out;
   a->last_state = p->last_state;
   a->chunk_states = p->chunk_states;
+  a->h_init = p->initial_state;
   a->batch = p->batch;
   a->dim = p->dim;
   a->L = p->seqlen;
@@ -129,6 +130,7 @@ int run_bwd(const mb200_scan_bwd_params* p, ScanArgs f, char* ws, const BwdLayou
   a.du = p->du;
   a.ddelta = p->ddelta;
   a.dz = p->dz;
+  a.dh_init = p->dinitial_state;
   a.part_bc = reinterpret_cast<float*>(ws + w.part_bc);
   a.part_A = batch_partials ? pA : reinterpret_cast<float*>(ws + w.part_A);
   a.part_D = batch_partials ? pD : reinterpret_cast<float*>(ws + w.part_D);
@@ -427,7 +429,7 @@ MB200_API const char* mb200_status_string(int status) {
   }
 }
 
-MB200_API int mb200_version(void) { return (1 << 16) | 0; }
+MB200_API int mb200_version(void) { return (1 << 16) | 1; }
 
 MB200_API int mb200_last_launch_count(void) { return g_launches; }
 

@@ -23,6 +23,7 @@ struct ScanArgs {
   void* out;            // forward output (io dtype), NULL in the states-only pass
   float* last_state;    // (batch, dim, dstate) or NULL
   float* chunk_states;  // (batch, dim, nchunks, dstate) or NULL
+  const float* h_init;  // (batch, dim, dstate) state before the first step, or NULL (zeros)
   int64_t batch, dim, L, N, ngroups, dpg;
   int64_t sBb, sBg, sBn, sBl, sCb, sCg, sCn, sCl;
   int tiles;    // CTAs per (batch, group) slice
@@ -40,6 +41,7 @@ struct BwdArgs {
   void* du;
   void* ddelta;
   void* dz;
+  float* dh_init;   // (batch, dim, dstate) gradient with respect to f.h_init, or NULL
   float* part_bc;   // (batch*ngroups, clusters, 2, N, Lpad) cluster partial sums of dB | dC
   float* part_A;    // (batch, dim, N)
   float* part_D;    // (batch, dim)

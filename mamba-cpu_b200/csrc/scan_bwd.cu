@@ -136,6 +136,8 @@ __device__ __forceinline__ void bwd_chunk(const BwdArgs& a, BwdSmem<TW, kBwdWarp
           hck[j] = sm.hst[buf][cl_c][n];
         else
           hck[j] = a.states[(row * f.nchunks + (k - 1)) * N + n];
+      } else if (k == 0 && valid && live && f.h_init != nullptr) {
+        hck[j] = f.h_init[row * N + n];
       }
       if (!live) {
 #pragma unroll
@@ -544,6 +546,19 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3) scan_bwd_kernel(const BwdAr
     // next iteration may refill it.
   }
 
+  // -- the adjoint entering the first step is the gradient of the initial state (every segment
+  //    lane of a channel holds it)
+  if (a.dh_init != nullptr) {
+    float ghp[kMaxState];
+    tmem_wait_st();
+    tmem_ld16(tcar, ghp);
+    tmem_wait_ld();
+    if (valid && s == 0) {
+#pragma unroll
+      for (int n = 0; n < kMaxState; ++n)
+        if (n < N) a.dh_init[row * N + n] = ghp[n];
+    }
+  }
   // -- per-row partials of dA / dD / ddelta_bias: sum the S segment lanes of the channel
   {
     float dAp[kMaxState];

@@ -176,8 +176,8 @@ __global__ void __launch_bounds__(kThreads, 3) scan_fwd_kernel(const ScanArgs a)
     const int n = p + j * Sh::kLPC;
     Aj[j] = (lvalid && n < N) ? a.A[(d0 + cl) * N + n] : 0.f;
     A2[j] = make_float2(Aj[j] * kLog2e, Aj[j] * kLog2e);
-    h[j] = 0.f;
-    h0[j] = 0.f;
+    h[j] = (lvalid && n < N && a.h_init != nullptr) ? a.h_init[(row0 + cl) * N + n] : 0.f;
+    h0[j] = h[j];
     P[j] = make_float2(1.f, 1.f);
   }
   float2 sd = make_float2(0.f, 0.f);

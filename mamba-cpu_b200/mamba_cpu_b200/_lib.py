@@ -44,7 +44,7 @@ _i32 = ctypes.c_int32
 class ScanFwdParams(ctypes.Structure):
     _fields_ = [
         ("u", _vp), ("delta", _vp), ("A", _vp), ("B", _vp), ("C", _vp), ("D", _vp), ("z", _vp),
-        ("delta_bias", _vp), ("out", _vp), ("last_state", _vp), ("chunk_states", _vp),
+        ("delta_bias", _vp), ("out", _vp), ("last_state", _vp), ("chunk_states", _vp), ("initial_state", _vp),
         ("batch", _i64), ("dim", _i64), ("seqlen", _i64), ("dstate", _i64), ("ngroups", _i64),
         ("B_batch_stride", _i64), ("B_group_stride", _i64), ("B_dstate_stride", _i64),
         ("B_seqlen_stride", _i64),
@@ -58,7 +58,7 @@ class ScanBwdParams(ctypes.Structure):
     _fields_ = [
         ("fwd", ScanFwdParams),
         ("dout", _vp), ("dlast_state", _vp), ("du", _vp), ("ddelta", _vp), ("dz", _vp), ("dA", _vp),
-        ("dB", _vp), ("dC", _vp), ("dD", _vp), ("ddelta_bias", _vp),
+        ("dB", _vp), ("dC", _vp), ("dD", _vp), ("ddelta_bias", _vp), ("dinitial_state", _vp),
         ("dbc_dtype", _i32), ("reserved", _i32),
     ]
 

@@ -81,17 +81,28 @@ def _selective_scan_fwd(
     delta_softplus: bool,
 ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
     """Returns (out in u's dtype, last_state float32 (b, d, n), chunk_states float32 (b, d, c, n))."""
-    _check_op_inputs("mamba_b200::selective_scan_fwd", u, delta, A, B, C, D, z, delta_bias)
+    return _run_fwd("mamba_b200::selective_scan_fwd", u, delta, A, B, C, D, z, delta_bias, delta_softplus, None)
+
+
+def _check_state(name, what, t, batch, dim, dstate):
+    if t is not None and (t.dtype != torch.float32 or not t.is_contiguous() or t.shape != (batch, dim, dstate)):
+        raise ValueError(f"{name}: {what} must be contiguous float32 (batch, dim, dstate)")
+
+
+def _run_fwd(name, u, delta, A, B, C, D, z, delta_bias, delta_softplus, initial_state):
+    _check_op_inputs(name, u, delta, A, B, C, D, z, delta_bias)
     batch, dim, seqlen = u.shape
     dstate = B.shape[2]
+    _check_state(name, "initial_state", initial_state, batch, dim, dstate)
     out = torch.empty_like(u)
     last_state = u.new_empty(batch, dim, dstate, dtype=torch.float32)
     chunk_states = u.new_empty(batch, dim, _nchunks(seqlen), dstate, dtype=torch.float32)
     p = _fwd_params(u, delta, A, B, C, D, z, delta_bias, delta_softplus)
     p.out, p.last_state, p.chunk_states = _lib.ptr(out), _lib.ptr(last_state), _lib.ptr(chunk_states)
+    p.initial_state = _lib.ptr(initial_state)
     with torch.cuda.device(u.device):
         st = _lib.lib.mb200_selective_scan_fwd(p, _lib.stream_of(u))
-    _lib.check(st, "mamba_b200::selective_scan_fwd")
+    _lib.check(st, name)
     return out, last_state, chunk_states
 
 
@@ -129,17 +140,23 @@ def _selective_scan_bwd(
     du/ddelta/dz are in u's dtype, dB/dC float32 in B's shape (contiguous), dA/dD/ddelta_bias
     float32 summed over batch. dz is empty when z is None; dD and ddelta_bias are always
     computed, as in the reference (selective_scan_interface.py:65-66)."""
-    _check_op_inputs("mamba_b200::selective_scan_bwd", u, delta, A, B, C, D, z, delta_bias)
+    return _run_bwd("mamba_b200::selective_scan_bwd", u, delta, A, B, C, D, z, delta_bias, delta_softplus, dout,
+                    dlast_state, chunk_states, None)[:8]
+
+
+def _run_bwd(name, u, delta, A, B, C, D, z, delta_bias, delta_softplus, dout, dlast_state, chunk_states,
+             initial_state):
+    _check_op_inputs(name, u, delta, A, B, C, D, z, delta_bias)
     if dout.shape != u.shape or dout.dtype != u.dtype or not dout.is_contiguous():
-        raise ValueError("mamba_b200::selective_scan_bwd: dout must be contiguous with u's shape and dtype")
+        raise ValueError(f"{name}: dout must be contiguous with u's shape and dtype")
     batch, dim, seqlen = u.shape
     dstate = B.shape[2]
     if dlast_state is not None and (dlast_state.dtype != torch.float32 or not dlast_state.is_contiguous()
                                     or dlast_state.shape != (batch, dim, dstate)):
-        raise ValueError("mamba_b200::selective_scan_bwd: dlast_state must be contiguous float32 (b, d, n)")
+        raise ValueError(f"{name}: dlast_state must be contiguous float32 (b, d, n)")
     if chunk_states is not None and (chunk_states.dtype != torch.float32 or not chunk_states.is_contiguous()
                                      or chunk_states.shape != (batch, dim, _nchunks(seqlen), dstate)):
-        raise ValueError("mamba_b200::selective_scan_bwd: chunk_states must come from selective_scan_fwd")
+        raise ValueError(f"{name}: chunk_states must come from selective_scan_fwd")
     du = torch.empty_like(u)
     ddelta = torch.empty_like(delta)
     dA = torch.empty_like(A)
@@ -148,9 +165,13 @@ def _selective_scan_bwd(
     dD = u.new_empty(dim, dtype=torch.float32)
     dz = torch.empty_like(z) if z is not None else u.new_empty(0)
     ddelta_bias = u.new_empty(dim, dtype=torch.float32)
+    _check_state(name, "initial_state", initial_state, batch, dim, dstate)
+    dinit = u.new_empty(batch, dim, dstate, dtype=torch.float32) if initial_state is not None else u.new_empty(0)
     p = _lib.ScanBwdParams()
     p.fwd = _fwd_params(u, delta, A, B, C, D, z, delta_bias, delta_softplus)
     p.fwd.chunk_states = _lib.ptr(chunk_states)
+    p.fwd.initial_state = _lib.ptr(initial_state)
+    p.dinitial_state = _lib.ptr(dinit) if initial_state is not None else None
     p.dout, p.dlast_state = _lib.ptr(dout), _lib.ptr(dlast_state)
     p.du, p.ddelta, p.dz = _lib.ptr(du), _lib.ptr(ddelta), (_lib.ptr(dz) if z is not None else None)
     p.dA, p.dB, p.dC, p.dD, p.ddelta_bias = (_lib.ptr(dA), _lib.ptr(dB), _lib.ptr(dC), _lib.ptr(dD),
@@ -160,8 +181,8 @@ def _selective_scan_bwd(
     ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=u.device)
     with torch.cuda.device(u.device):
         st = _lib.lib.mb200_selective_scan_bwd(p, _lib.ptr(ws), nbytes, _lib.stream_of(u))
-    _lib.check(st, "mamba_b200::selective_scan_bwd")
-    return du, ddelta, dA, dB, dC, dD, dz, ddelta_bias
+    _lib.check(st, name)
+    return du, ddelta, dA, dB, dC, dD, dz, ddelta_bias, dinit
 
 
 @_selective_scan_bwd.register_fake
@@ -206,6 +227,107 @@ def _backward(ctx, grad_out, grad_last_state, grad_chunk_states):
 
 torch.library.register_autograd(
     "mamba_b200::selective_scan_fwd", _backward, setup_context=_setup_context
+)
+
+
+# ---- variants with an initial state (a sequence scanned in pieces, e.g. across GPUs) ----------
+# No reference counterpart: the reference always starts from a zero state. The kernels are the
+# same; the state before the first step comes from `initial_state` (batch, dim, dstate) fp32,
+# and the backward also returns the gradient with respect to it.
+
+
+@torch.library.custom_op("mamba_b200::selective_scan_fwd_init", mutates_args=(), device_types="cuda")
+def _selective_scan_fwd_init(
+    u: torch.Tensor,
+    delta: torch.Tensor,
+    A: torch.Tensor,
+    B: torch.Tensor,
+    C: torch.Tensor,
+    D: Optional[torch.Tensor],
+    z: Optional[torch.Tensor],
+    delta_bias: Optional[torch.Tensor],
+    delta_softplus: bool,
+    initial_state: torch.Tensor,
+) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """selective_scan_fwd starting from initial_state instead of zeros."""
+    return _run_fwd("mamba_b200::selective_scan_fwd_init", u, delta, A, B, C, D, z, delta_bias, delta_softplus,
+                    initial_state)
+
+
+@_selective_scan_fwd_init.register_fake
+def _(u, delta, A, B, C, D, z, delta_bias, delta_softplus, initial_state):
+    batch, dim, seqlen = u.shape
+    dstate = B.shape[2]
+    return (
+        torch.empty_like(u),
+        u.new_empty(batch, dim, dstate, dtype=torch.float32),
+        u.new_empty(batch, dim, _nchunks(seqlen), dstate, dtype=torch.float32),
+    )
+
+
+@torch.library.custom_op("mamba_b200::selective_scan_bwd_init", mutates_args=(), device_types="cuda")
+def _selective_scan_bwd_init(
+    u: torch.Tensor,
+    delta: torch.Tensor,
+    A: torch.Tensor,
+    B: torch.Tensor,
+    C: torch.Tensor,
+    D: Optional[torch.Tensor],
+    z: Optional[torch.Tensor],
+    delta_bias: Optional[torch.Tensor],
+    delta_softplus: bool,
+    dout: torch.Tensor,
+    dlast_state: Optional[torch.Tensor],
+    chunk_states: Optional[torch.Tensor],
+    initial_state: torch.Tensor,
+) -> tuple[
+    torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor,
+    torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor,
+]:
+    """selective_scan_bwd of selective_scan_fwd_init: the eight gradients plus dinitial_state."""
+    return _run_bwd("mamba_b200::selective_scan_bwd_init", u, delta, A, B, C, D, z, delta_bias, delta_softplus,
+                    dout, dlast_state, chunk_states, initial_state)
+
+
+@_selective_scan_bwd_init.register_fake
+def _(u, delta, A, B, C, D, z, delta_bias, delta_softplus, dout, dlast_state, chunk_states, initial_state):
+    dim = u.shape[1]
+    return (
+        torch.empty_like(u), torch.empty_like(delta), torch.empty_like(A),
+        u.new_empty(B.shape, dtype=torch.float32), u.new_empty(C.shape, dtype=torch.float32),
+        u.new_empty(dim, dtype=torch.float32),
+        torch.empty_like(z) if z is not None else u.new_empty(0),
+        u.new_empty(dim, dtype=torch.float32),
+        torch.empty_like(initial_state),
+    )
+
+
+def _setup_context_init(ctx, inputs, output):
+    u, delta, A, B, C, D, z, delta_bias, delta_softplus, initial_state = inputs
+    _, _, chunk_states = output
+    ctx.save_for_backward(u, delta, A, B, C, D, z, delta_bias, chunk_states, initial_state)
+    ctx.delta_softplus = delta_softplus
+
+
+def _backward_init(ctx, grad_out, grad_last_state, grad_chunk_states):
+    u, delta, A, B, C, D, z, delta_bias, chunk_states, initial_state = ctx.saved_tensors
+    dout = torch.zeros_like(u) if grad_out is None else grad_out.to(u.dtype).contiguous()
+    dlast = None if grad_last_state is None else grad_last_state.float().contiguous()
+    du, ddelta, dA, dB, dC, dD, dz, ddelta_bias, dinit = torch.ops.mamba_b200.selective_scan_bwd_init(
+        u, delta, A, B, C, D, z, delta_bias, ctx.delta_softplus, dout, dlast, chunk_states, initial_state
+    )
+    return (
+        du, ddelta, dA, dB.to(B.dtype), dC.to(C.dtype),
+        dD if D is not None else None,
+        dz if z is not None else None,
+        ddelta_bias if delta_bias is not None else None,
+        None,
+        dinit,
+    )
+
+
+torch.library.register_autograd(
+    "mamba_b200::selective_scan_fwd_init", _backward_init, setup_context=_setup_context_init
 )
 
 

@@ -113,3 +113,121 @@ def world_of(group) -> Optional[int]:
     import torch.distributed as dist
 
     return dist.get_world_size(group) if group is not None else None
+
+
+# ---- sequence sharding ---------------------------------------------------------------------
+# A sequence too long for one GPU is split along seqlen: rank r holds timesteps
+# [r * L_r, (r + 1) * L_r) of u, delta, z, B, C (all ranks: every channel; A, D, delta_bias
+# replicated). The recurrence h_t = a_t h_{t-1} + b_t is linear in its initial state, so a rank's
+# piece maps an incoming state h to P h + e, with P = prod_t a_t = exp(A * sum_t dt) and e the
+# piece's end state from h = 0. Forward: every rank scans its piece from zero, the ranks
+# all-gather (P, e), rank r composes the pieces before it into its true initial state and scans
+# again from it (rank 0's first pass is already exact). The backward mirrors this with the
+# adjoint, which enters a piece from the right: a rank's piece maps an incoming adjoint g to
+# P g + f, f being the adjoint at the piece start for g = 0. dB / dC belong to the rank's own
+# timesteps; dA, dD and ddelta_bias are sums over time and are all-reduced. Cost: about two scans
+# per rank and direction, one all-gather of 2 x (batch, dim, dstate) fp32 per direction.
+
+
+def _piece_decay(delta, A, delta_bias, delta_softplus):
+    dt = delta.float()
+    if delta_bias is not None:
+        dt = dt + delta_bias.float()[:, None]
+    if delta_softplus:
+        dt = torch.nn.functional.softplus(dt)
+    return torch.exp(A.float()[None] * dt.sum(-1)[..., None])  # (batch, dim, dstate)
+
+
+def _all_gather_pair(P, e, group):
+    import torch.distributed as dist
+
+    world = dist.get_world_size(group)
+    stacked = torch.stack([P, e]).contiguous()
+    out = [torch.empty_like(stacked) for _ in range(world)]
+    dist.all_gather(out, stacked, group=group)
+    return out
+
+
+class _SeqShardedScan(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, u, delta, A, B, C, D, z, delta_bias, delta_softplus, group):
+        import torch.distributed as dist
+
+        ops = torch.ops.mamba_b200
+        rank, world = dist.get_rank(group), dist.get_world_size(group)
+        b, d, _ = u.shape
+        n = A.shape[-1]
+        zero = torch.zeros(b, d, n, dtype=torch.float32, device=u.device)
+        out, last, cs = ops.selective_scan_fwd_init(u, delta, A, B, C, D, z, delta_bias, delta_softplus, zero)
+        P = _piece_decay(delta, A, delta_bias, delta_softplus)
+        pieces = _all_gather_pair(P, last, group)
+        h0 = zero
+        for q in range(rank):
+            h0 = pieces[q][0] * h0 + pieces[q][1]
+        h0 = h0.contiguous()
+        if rank > 0:
+            out, last, cs = ops.selective_scan_fwd_init(u, delta, A, B, C, D, z, delta_bias, delta_softplus, h0)
+        ctx.save_for_backward(u, delta, A, B, C, D, z, delta_bias, cs, h0, P)
+        ctx.delta_softplus = delta_softplus
+        ctx.group = group
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        import torch.distributed as dist
+
+        ops = torch.ops.mamba_b200
+        u, delta, A, B, C, D, z, delta_bias, cs, h0, P = ctx.saved_tensors
+        group = ctx.group
+        rank, world = dist.get_rank(group), dist.get_world_size(group)
+        dout = dout.to(u.dtype).contiguous()
+        args = (u, delta, A, B, C, D, z, delta_bias, ctx.delta_softplus, dout)
+        grads = ops.selective_scan_bwd_init(*args, None, cs, h0)
+        pieces = _all_gather_pair(P, grads[8], group)
+        g = torch.zeros_like(h0)
+        for q in range(world - 1, rank, -1):
+            g = pieces[q][0] * g + pieces[q][1]
+        if rank < world - 1:
+            grads = ops.selective_scan_bwd_init(*args, g.contiguous(), cs, h0)
+        du, ddelta, dA, dB, dC, dD, dz, ddelta_bias, _ = grads
+        flat = torch.cat([dA.reshape(-1), dD, ddelta_bias])
+        dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=group)
+        dA = flat[:dA.numel()].view_as(dA)
+        dD = flat[dA.numel():dA.numel() + dD.numel()]
+        ddelta_bias = flat[dA.numel() + dD.numel():]
+        return (du, ddelta, dA, dB.to(B.dtype), dC.to(C.dtype),
+                dD if D is not None else None, dz if z is not None else None,
+                ddelta_bias if delta_bias is not None else None, None, None)
+
+
+def selective_scan_seq_sharded(u, delta, A, B, C, D=None, z=None, delta_bias=None, delta_softplus=False,
+                               group=None):
+    """Selective scan of a sequence split along seqlen across the ranks of ``group``.
+
+    Each rank passes its own timesteps of u, delta, z (batch, dim, L_r) and B, C
+    ((batch, [ngroups,] dstate, L_r)), in rank order along the sequence, and the same A, D,
+    delta_bias. Returns this rank's piece of ``out`` (as ``selective_scan_fn`` would return it for
+    the whole sequence); gradients flow back through autograd (dA / dD / ddelta_bias summed over
+    all ranks). Collectives: one all-gather per direction plus one all-reduce in the backward.
+    """
+    import torch.distributed as dist
+
+    if group is None:
+        group = dist.group.WORLD
+    if u.device.type != "cuda":
+        raise ValueError(f"mamba_cpu_b200 runs on CUDA tensors, got device {u.device}")
+    if B.dim() == 3:
+        B = B.unsqueeze(1)
+    if C.dim() == 3:
+        C = C.unsqueeze(1)
+    io = u.dtype if u.dtype in (torch.float32, torch.bfloat16, torch.float16) else torch.float32
+    Bk, Ck = B.to(io if B.dtype == io else torch.float32), C.to(io if C.dtype == io else torch.float32)
+    if Bk.dtype != Ck.dtype:
+        Bk, Ck = Bk.float(), Ck.float()
+    Bk = Bk if Bk.stride(-1) == 1 else Bk.contiguous()
+    Ck = Ck if Ck.stride(-1) == 1 else Ck.contiguous()
+    out = _SeqShardedScan.apply(
+        u.to(io).contiguous(), delta.to(io).contiguous(), A.float().contiguous(), Bk, Ck,
+        None if D is None else D.float().contiguous(), None if z is None else z.to(io).contiguous(),
+        None if delta_bias is None else delta_bias.float().contiguous(), bool(delta_softplus), group)
+    return out.to(u.dtype)

@@ -26,6 +26,10 @@ def _load():
         lib.oracle_scan_fwd.restype = ctypes.c_int
         lib.oracle_scan_bwd.argtypes = [_P] * 18 + [_I] * 5 + [ctypes.c_int]
         lib.oracle_scan_bwd.restype = ctypes.c_int
+        lib.oracle_scan_fwd_init.argtypes = [_P] * 11 + [_I] * 5 + [ctypes.c_int]
+        lib.oracle_scan_fwd_init.restype = ctypes.c_int
+        lib.oracle_scan_bwd_init.argtypes = [_P] * 20 + [_I] * 5 + [ctypes.c_int]
+        lib.oracle_scan_bwd_init.restype = ctypes.c_int
         lib.oracle_conv1d_fwd.argtypes = [_P] * 6 + [_I] * 4 + [ctypes.c_int]
         lib.oracle_conv1d_fwd.restype = ctypes.c_int
         lib.oracle_conv1d_bwd.argtypes = [_P] * 9 + [_I] * 4 + [ctypes.c_int]
@@ -65,29 +69,31 @@ def _bc(X):
     return X[:, None] if X.ndim == 3 else X
 
 
-def scan_fwd(u, delta, A, B, C, D=None, z=None, delta_bias=None, delta_softplus=False):
-    """Returns (out, last_state) in float64."""
-    u, delta, A, D, z, delta_bias = map(_f32, (u, delta, A, D, z, delta_bias))
+def scan_fwd(u, delta, A, B, C, D=None, z=None, delta_bias=None, delta_softplus=False, initial_state=None):
+    """Returns (out, last_state) in float64. initial_state (batch, dim, dstate): the state before
+    the first step (zeros when None)."""
+    u, delta, A, D, z, delta_bias, h0 = map(_f32, (u, delta, A, D, z, delta_bias, initial_state))
     B, C = _bc(B), _bc(C)
     batch, dim, seqlen = u.shape
     ngroups, dstate = B.shape[1], B.shape[2]
     out = np.empty((batch, dim, seqlen), np.float64)
     last = np.empty((batch, dim, dstate), np.float64)
-    rc = _load().oracle_scan_fwd(
-        _ptr(u), _ptr(delta), _ptr(A), _ptr(B), _ptr(C), _ptr(D), _ptr(z), _ptr(delta_bias),
+    rc = _load().oracle_scan_fwd_init(
+        _ptr(u), _ptr(delta), _ptr(A), _ptr(B), _ptr(C), _ptr(D), _ptr(z), _ptr(delta_bias), _ptr(h0),
         _ptr(out), _ptr(last), batch, dim, seqlen, dstate, ngroups, int(bool(delta_softplus)))
     if rc:
         raise ValueError(f"oracle_scan_fwd rejected its arguments (status {rc})")
     return out, last
 
 
-def scan_bwd(u, delta, A, B, C, D, z, delta_bias, delta_softplus, dout, dlast_state=None):
-    """Returns a dict with du, ddelta, dA, dB, dC, dD, dz (None without z), ddelta_bias.
+def scan_bwd(u, delta, A, B, C, D, z, delta_bias, delta_softplus, dout, dlast_state=None, initial_state=None):
+    """Returns a dict with du, ddelta, dA, dB, dC, dD, dz (None without z), ddelta_bias and
+    dinitial_state (the gradient with respect to initial_state, (batch, dim, dstate)).
 
     dA/dD/ddelta_bias are summed over batch (selective_scan_interface.py:87); dB/dC have B's
     (batch, ngroups, dstate, seqlen) shape (3-D B gives a 4-D result with ngroups = 1)."""
-    u, delta, A, D, z, delta_bias, dout, dlast_state = map(
-        _f32, (u, delta, A, D, z, delta_bias, dout, dlast_state))
+    u, delta, A, D, z, delta_bias, dout, dlast_state, h0 = map(
+        _f32, (u, delta, A, D, z, delta_bias, dout, dlast_state, initial_state))
     B, C = _bc(B), _bc(C)
     batch, dim, seqlen = u.shape
     ngroups, dstate = B.shape[1], B.shape[2]
@@ -99,14 +105,15 @@ def scan_bwd(u, delta, A, B, C, D, z, delta_bias, delta_softplus, dout, dlast_st
     dC = np.empty(C.shape, np.float64)
     dD = np.empty((dim,), np.float64)
     db = np.empty((dim,), np.float64)
-    rc = _load().oracle_scan_bwd(
-        _ptr(u), _ptr(delta), _ptr(A), _ptr(B), _ptr(C), _ptr(D), _ptr(z), _ptr(delta_bias),
+    dh0 = np.empty((batch, dim, dstate), np.float64)
+    rc = _load().oracle_scan_bwd_init(
+        _ptr(u), _ptr(delta), _ptr(A), _ptr(B), _ptr(C), _ptr(D), _ptr(z), _ptr(delta_bias), _ptr(h0),
         _ptr(dout), _ptr(dlast_state), _ptr(du), _ptr(ddelta), _ptr(dA), _ptr(dB), _ptr(dC),
-        _ptr(dD), _ptr(dz), _ptr(db), batch, dim, seqlen, dstate, ngroups,
+        _ptr(dD), _ptr(dz), _ptr(db), _ptr(dh0), batch, dim, seqlen, dstate, ngroups,
         int(bool(delta_softplus)))
     if rc:
         raise ValueError(f"oracle_scan_bwd rejected its arguments (status {rc})")
-    return dict(du=du, ddelta=ddelta, dA=dA, dB=dB, dC=dC, dD=dD, dz=dz, ddelta_bias=db)
+    return dict(du=du, ddelta=ddelta, dA=dA, dB=dB, dC=dC, dD=dD, dz=dz, ddelta_bias=db, dinitial_state=dh0)
 
 
 def conv1d_fwd(x, weight, bias=None, initial_states=None, activation=None, return_final_states=False):

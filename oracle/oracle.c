@@ -101,7 +101,7 @@ static double row_dt(const float* delta_row, double bias, int64_t t, int softplu
 
 /* Forward: selective_scan.cpp:120-145. out and last_state are float64. */
 typedef struct {
-  const float *u, *delta, *A, *B, *C, *D, *z, *delta_bias;
+  const float *u, *delta, *A, *B, *C, *D, *z, *delta_bias, *h_init;
   double *out, *last_state;
   int64_t batch, dim, seqlen, dstate, ngroups;
   int softplus;
@@ -121,7 +121,7 @@ static void fwd_rows(int64_t lo, int64_t hi, void* vctx) {
     const float* Cs = c->C + slice * N * L;
     const double Dd = c->D ? (double)c->D[d] : 0.0;
     const double bias = c->delta_bias ? (double)c->delta_bias[d] : 0.0;
-    for (int64_t n = 0; n < N; ++n) h[n] = 0.0;
+    for (int64_t n = 0; n < N; ++n) h[n] = c->h_init ? (double)c->h_init[idx * N + n] : 0.0;
     for (int64_t t = 0; t < L; ++t) {
       const double dt = row_dt(dr, bias, t, c->softplus);
       const double dtu = dt * (double)ur[t];
@@ -142,15 +142,25 @@ static void fwd_rows(int64_t lo, int64_t hi, void* vctx) {
   }
 }
 
+/* h_init: (batch, dim, dstate) state before the first step, or NULL for zeros (an extension of
+ * the reference, which always starts from zero; used to check sequence-sharded scans). */
+int oracle_scan_fwd_init(const float* u, const float* delta, const float* A, const float* B,
+                         const float* C, const float* D, const float* z, const float* delta_bias,
+                         const float* h_init, double* out, double* last_state, int64_t batch,
+                         int64_t dim, int64_t seqlen, int64_t dstate, int64_t ngroups, int softplus) {
+  if (dstate > 256 || ngroups <= 0 || dim % ngroups) return 1;
+  fwd_ctx c = {u, delta, A, B, C, D, z, delta_bias, h_init, out, last_state,
+               batch, dim, seqlen, dstate, ngroups, softplus};
+  parallel_for(batch * dim, fwd_rows, &c);
+  return 0;
+}
+
 int oracle_scan_fwd(const float* u, const float* delta, const float* A, const float* B,
                     const float* C, const float* D, const float* z, const float* delta_bias,
                     double* out, double* last_state, int64_t batch, int64_t dim, int64_t seqlen,
                     int64_t dstate, int64_t ngroups, int softplus) {
-  if (dstate > 256 || ngroups <= 0 || dim % ngroups) return 1;
-  fwd_ctx c = {u, delta, A, B, C, D, z, delta_bias, out, last_state,
-               batch, dim, seqlen, dstate, ngroups, softplus};
-  parallel_for(batch * dim, fwd_rows, &c);
-  return 0;
+  return oracle_scan_fwd_init(u, delta, A, B, C, D, z, delta_bias, NULL, out, last_state, batch, dim,
+                              seqlen, dstate, ngroups, softplus);
 }
 
 /*
@@ -167,8 +177,8 @@ int oracle_scan_fwd(const float* u, const float* delta, const float* A, const fl
 #define BWD_BLOCKS_PER_SLICE 16
 
 typedef struct {
-  const float *u, *delta, *A, *B, *C, *D, *z, *delta_bias, *dout, *dlast;
-  double *du, *ddelta, *dz;
+  const float *u, *delta, *A, *B, *C, *D, *z, *delta_bias, *dout, *dlast, *h_init;
+  double *du, *ddelta, *dz, *dh_init;
   double *dA_part, *dD_part, *db_part; /* per row */
   double* blk;                          /* (slices, blocks, 2, N, L) */
   int64_t batch, dim, seqlen, dstate, ngroups, blocks;
@@ -204,7 +214,7 @@ static void bwd_blocks(int64_t lo, int64_t hi, void* vctx) {
         const double dt = row_dt(dr, bias, t, c->softplus);
         const double dtu = dt * (double)ur[t];
         for (int64_t n = 0; n < N; ++n) {
-          const double hp = t > 0 ? hs[(t - 1) * N + n] : 0.0;
+          const double hp = t > 0 ? hs[(t - 1) * N + n] : (c->h_init ? (double)c->h_init[idx * N + n] : 0.0);
           hs[t * N + n] = exp(dt * (double)Ar[n]) * hp + dtu * (double)Bs[n * L + t];
         }
       }
@@ -234,7 +244,7 @@ static void bwd_blocks(int64_t lo, int64_t hi, void* vctx) {
         for (int64_t n = 0; n < N; ++n) {
           const double Bn = (double)Bs[n * L + t];
           const double Cn = (double)Cs[n * L + t];
-          const double hp = t > 0 ? hs[(t - 1) * N + n] : 0.0;
+          const double hp = t > 0 ? hs[(t - 1) * N + n] : (c->h_init ? (double)c->h_init[idx * N + n] : 0.0);
           const double g = gh[n] + dy * Cn;
           dCs[n * L + t] += dy * h[n];
           const double a = exp(dt * (double)Ar[n]);
@@ -251,6 +261,8 @@ static void bwd_blocks(int64_t lo, int64_t hi, void* vctx) {
         dbias_acc += ddt;
       }
       for (int64_t n = 0; n < N; ++n) c->dA_part[idx * N + n] = dA_acc[n];
+      if (c->dh_init)
+        for (int64_t n = 0; n < N; ++n) c->dh_init[idx * N + n] = gh[n];
       c->dD_part[idx] = dD_acc;
       c->db_part[idx] = dbias_acc;
     }
@@ -258,12 +270,14 @@ static void bwd_blocks(int64_t lo, int64_t hi, void* vctx) {
   free(hs);
 }
 
-int oracle_scan_bwd(const float* u, const float* delta, const float* A, const float* B,
-                    const float* C, const float* D, const float* z, const float* delta_bias,
-                    const float* dout, const float* dlast_state, double* du, double* ddelta,
-                    double* dA, double* dB, double* dC, double* dD, double* dz,
-                    double* ddelta_bias, int64_t batch, int64_t dim, int64_t seqlen,
-                    int64_t dstate, int64_t ngroups, int softplus) {
+/* h_init as in oracle_scan_fwd_init; dh_init (batch, dim, dstate) receives the gradient with
+ * respect to it (may be NULL). */
+int oracle_scan_bwd_init(const float* u, const float* delta, const float* A, const float* B,
+                         const float* C, const float* D, const float* z, const float* delta_bias,
+                         const float* h_init, const float* dout, const float* dlast_state, double* du,
+                         double* ddelta, double* dA, double* dB, double* dC, double* dD, double* dz,
+                         double* ddelta_bias, double* dh_init, int64_t batch, int64_t dim,
+                         int64_t seqlen, int64_t dstate, int64_t ngroups, int softplus) {
   if (dstate > 256 || ngroups <= 0 || dim % ngroups) return 1;
   const int64_t L = seqlen, N = dstate;
   const int64_t rows = batch * dim;
@@ -272,8 +286,8 @@ int oracle_scan_bwd(const float* u, const float* delta, const float* A, const fl
   const int64_t blocks = dpg < BWD_BLOCKS_PER_SLICE ? (dpg > 0 ? dpg : 1) : BWD_BLOCKS_PER_SLICE;
   bwd_ctx c;
   c.u = u; c.delta = delta; c.A = A; c.B = B; c.C = C; c.D = D; c.z = z;
-  c.delta_bias = delta_bias; c.dout = dout; c.dlast = dlast_state;
-  c.du = du; c.ddelta = ddelta; c.dz = dz;
+  c.delta_bias = delta_bias; c.dout = dout; c.dlast = dlast_state; c.h_init = h_init;
+  c.du = du; c.ddelta = ddelta; c.dz = dz; c.dh_init = dh_init;
   c.dA_part = (double*)calloc((size_t)(rows * N + 1), sizeof(double));
   c.dD_part = (double*)calloc((size_t)(rows + 1), sizeof(double));
   c.db_part = (double*)calloc((size_t)(rows + 1), sizeof(double));
@@ -311,6 +325,17 @@ int oracle_scan_bwd(const float* u, const float* delta, const float* A, const fl
   }
   free(c.dA_part); free(c.dD_part); free(c.db_part); free(c.blk);
   return 0;
+}
+
+int oracle_scan_bwd(const float* u, const float* delta, const float* A, const float* B,
+                    const float* C, const float* D, const float* z, const float* delta_bias,
+                    const float* dout, const float* dlast_state, double* du, double* ddelta,
+                    double* dA, double* dB, double* dC, double* dD, double* dz,
+                    double* ddelta_bias, int64_t batch, int64_t dim, int64_t seqlen,
+                    int64_t dstate, int64_t ngroups, int softplus) {
+  return oracle_scan_bwd_init(u, delta, A, B, C, D, z, delta_bias, NULL, dout, dlast_state, du, ddelta,
+                              dA, dB, dC, dD, dz, ddelta_bias, NULL, batch, dim, seqlen, dstate, ngroups,
+                              softplus);
 }
 
 /* ---- causal depthwise conv1d: ops/causal_conv1d.py:16-53 ------------------------------- */

@@ -178,3 +178,89 @@ def test_all_reduce_bc_is_one_sum_over_ranks(tmp_path):
         got = np.load(tmp_path / f"r{r}.npz")
         np.testing.assert_array_equal(got["dB"], np.full((2, 1, 3, 5), 3.0, np.float32))
         np.testing.assert_array_equal(got["dC"], np.arange(30, dtype=np.float32).reshape(2, 1, 3, 5) * 3)
+
+
+# ---- sequence sharding (parallel.selective_scan_seq_sharded) -------------------------------
+
+
+def _oracle_fwd_init(u, delta, A, B, C, D, z, delta_bias, softplus, initial_state):
+    from oracle import f64
+
+    out, last = f64.scan_fwd(u, delta, A, B, C, D, z, delta_bias, softplus, initial_state=initial_state)
+    return torch.from_numpy(out).float(), torch.from_numpy(last).float(), torch.zeros(1)
+
+
+def _oracle_bwd_init(u, delta, A, B, C, D, z, delta_bias, softplus, dout, dlast, chunk_states, initial_state):
+    from oracle import f64
+
+    r = f64.scan_bwd(u, delta, A, B, C, D, z, delta_bias, softplus, dout, dlast, initial_state=initial_state)
+    t = {k: torch.from_numpy(v).float() for k, v in r.items() if v is not None}
+    return (t["du"], t["ddelta"], t["dA"], t["dB"], t["dC"], t["dD"], t["dz"], t["ddelta_bias"],
+            t["dinitial_state"])
+
+
+def _seq_inputs(L):
+    g = torch.Generator().manual_seed(9)
+    b, d, n = 2, 6, 4
+    return dict(
+        u=torch.randn(b, d, L, generator=g),
+        delta=torch.rand(b, d, L, generator=g) * 0.5,
+        A=-torch.rand(d, n, generator=g) * 0.5 - 0.05,  # long memories: the pieces interact
+        B=torch.randn(b, 1, n, L, generator=g),
+        C=torch.randn(b, 1, n, L, generator=g),
+        D=torch.randn(d, generator=g),
+        z=torch.randn(b, d, L, generator=g),
+        delta_bias=torch.rand(d, generator=g) * 0.1,
+        dout=torch.randn(b, d, L, generator=g),
+    )
+
+
+def _seq_worker(rank, world, port, L, outdir):
+    import torch.distributed as dist
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    try:
+        x = _seq_inputs(L)
+        lo, hi = rank * L // world, (rank + 1) * L // world
+        piece = {k: (v[..., lo:hi].contiguous() if k in ("u", "delta", "z", "B", "C", "dout") else v.clone())
+                 for k, v in x.items()}
+        leaves = {k: piece[k].requires_grad_() for k in ("u", "delta", "A", "B", "C", "D", "z", "delta_bias")}
+        ops = torch.ops.mamba_b200
+        saved = {n: getattr(ops, n) for n in ("selective_scan_fwd_init", "selective_scan_bwd_init")}
+        setattr(ops, "selective_scan_fwd_init", _oracle_fwd_init)
+        setattr(ops, "selective_scan_bwd_init", _oracle_bwd_init)
+        try:
+            out = parallel._SeqShardedScan.apply(
+                leaves["u"], leaves["delta"], leaves["A"], leaves["B"], leaves["C"], leaves["D"], leaves["z"],
+                leaves["delta_bias"], True, dist.group.WORLD)
+            out.backward(piece["dout"])
+        finally:
+            for n, f in saved.items():
+                setattr(ops, n, f)
+        np.savez(os.path.join(outdir, f"seq{rank}.npz"), lo=lo, hi=hi, out=out.detach().numpy(),
+                 **{"d" + k: v.grad.numpy() for k, v in leaves.items()})
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.timeout(300)
+@pytest.mark.parametrize("world,L", [(2, 150), (3, 200)])
+def test_sequence_sharded_scan_equals_unsharded(tmp_path, world, L):
+    """Rank r holds timesteps [r L / W, (r + 1) L / W); the composed result equals the oracle's
+    scan of the whole sequence, outputs and all gradients."""
+    from oracle import f64
+
+    mp.start_processes(_seq_worker, args=(world, _free_port(), L, str(tmp_path)), nprocs=world, join=True,
+                       start_method="spawn")
+    x = _seq_inputs(L)
+    args = [x[k] for k in ("u", "delta", "A", "B", "C", "D", "z", "delta_bias")]
+    out, _ = f64.scan_fwd(*args, True)
+    want = f64.scan_bwd(*args, True, x["dout"])
+    for r in range(world):
+        p = np.load(tmp_path / f"seq{r}.npz")
+        lo, hi = int(p["lo"]), int(p["hi"])
+        np.testing.assert_allclose(p["out"], out[..., lo:hi], rtol=1e-5, atol=1e-5, err_msg="out")
+        for k, key in (("du", "du"), ("ddelta", "ddelta"), ("dz", "dz"), ("dB", "dB"), ("dC", "dC")):
+            np.testing.assert_allclose(p[k], want[key][..., lo:hi], rtol=1e-4, atol=1e-5, err_msg=k)
+        for k, key in (("dA", "dA"), ("dD", "dD"), ("ddelta_bias", "ddelta_bias")):
+            np.testing.assert_allclose(p[k], want[key], rtol=1e-4, atol=1e-5, err_msg=k)
