@@ -29,6 +29,7 @@
 #include <cooperative_groups.h>
 
 #include "scan.cuh"
+#include "quad.cuh"
 #include "segscan.cuh"
 #include "stage.cuh"
 #include "tmem.cuh"
@@ -60,13 +61,59 @@ struct BwdSmem {
   uint32_t tmem_base;
 };
 
+// A lane's K items of u, delta, dout and z for one chunk, as loaded (converted when used). With
+// 2-byte items the next chunk's items are loaded at the end of the current chunk's state loop,
+// so their latency overlaps the reductions and the output stage instead of stalling the next
+// chunk's start. With 4-byte items that costs more registers than it saves (measured): those
+// rows are prefetched into L2 one chunk ahead and loaded when the chunk starts.
+template <typename TI, int K>
+struct ChunkItems {
+  static constexpr bool kCarry = sizeof(TI) == 2;
+  Quad<TI> u[kCarry ? K / 4 : 1], d[kCarry ? K / 4 : 1], o[kCarry ? K / 4 : 1], z[kCarry ? K / 4 : 1];
+};
+
+template <typename TI, int K, bool HAS_Z>
+__device__ __forceinline__ void load_chunk_items(ChunkItems<TI, K>& it, const TI* urow, const TI* drow,
+                                                 const TI* dorow, const TI* zrow, int64_t t0, int64_t L, bool vec) {
+  if constexpr (ChunkItems<TI, K>::kCarry) {
+#pragma unroll
+    for (int q = 0; q < K / 4; ++q) {
+      const int64_t t = t0 + 4 * q;
+      if (vec) {
+        it.u[q] = ld_quad_stream(urow + t);
+        it.d[q] = ld_quad_stream(drow + t);
+        it.o[q] = ld_quad_stream(dorow + t);
+        if constexpr (HAS_Z) it.z[q] = ld_quad_stream(zrow + t);
+      } else {
+        it.u[q] = ld_quad_masked(urow, t, L, 1);
+        it.d[q] = ld_quad_masked(drow, t, L, 1);
+        it.o[q] = ld_quad_masked(dorow, t, L, 1);
+        if constexpr (HAS_Z) it.z[q] = ld_quad_masked(zrow, t, L, 1);
+      }
+    }
+  }
+}
+
+template <typename TI, int K>
+__device__ __forceinline__ void unpack_items(const Quad<TI> (&q)[K / 4], float (&x)[K]) {
+#pragma unroll
+  for (int i = 0; i < K / 4; ++i) {
+    const float4 v = to_float4(q[i]);
+    x[4 * i] = v.x;
+    x[4 * i + 1] = v.y;
+    x[4 * i + 2] = v.z;
+    x[4 * i + 3] = v.w;
+  }
+}
+
 template <typename TI, typename TW, int S, bool HAS_Z, bool STAGED, bool MASKED>
 __device__ __forceinline__ void bwd_chunk(const BwdArgs& a, BwdSmem<TW, kBwdWarps * (32 / S)>& sm, int buf, int k,
                                           int64_t row, int64_t slice, int64_t cluster_idx, int cl_c, bool valid,
                                           int lane, int warp, int c, int s, const TW* Bbase, const TW* Cbase,
                                           float Dv, float bias, const TI* urow, const TI* drow, const TI* dorow,
                                           const TI* zrow, float& dDacc, float& dbacc, int& rbuf,
-                                          uint32_t tcar, cg::cluster_group& cluster) {
+                                          uint32_t tcar, ChunkItems<TI, kChunk / S>& items, bool next_vec,
+                                          cg::cluster_group& cluster) {
   constexpr int K = kChunk / S;
   constexpr int CW = 32 / S;
   constexpr int R = ilog2(CW);
@@ -75,17 +122,24 @@ __device__ __forceinline__ void bwd_chunk(const BwdArgs& a, BwdSmem<TW, kBwdWarp
   const int N = (int)f.N;
   const int64_t t0 = (int64_t)k * kChunk + s * K;
 
-  // The lane's items. u / delta / dout / z are read again at the end of the chunk (L1 hits)
-  // instead of being kept live through the state loop.
+  // The lane's items (loaded by the previous chunk). u / delta / dout / z are read again at the
+  // end of the chunk (L1 hits) instead of being kept live through the state loop.
   float dt[K], dtu[K], dy[K], gB[K], xA[K];
   float y[HAS_Z ? K : 1];
   float sdt = 0.f;
   {
     float uu[K], dl[K], dO[K], zz[K];
-    load_items<TI, K>(urow, t0, L, !MASKED, 0.f, uu);
-    load_items<TI, K>(drow, t0, L, !MASKED, 0.f, dl);
-    load_items<TI, K>(dorow, t0, L, !MASKED, 0.f, dO);
-    if constexpr (HAS_Z) load_items<TI, K>(zrow, t0, L, !MASKED, 0.f, zz);
+    if constexpr (ChunkItems<TI, K>::kCarry) {
+      unpack_items<TI, K>(items.u, uu);
+      unpack_items<TI, K>(items.d, dl);
+      unpack_items<TI, K>(items.o, dO);
+      if constexpr (HAS_Z) unpack_items<TI, K>(items.z, zz);
+    } else {
+      load_items<TI, K>(urow, t0, L, !MASKED, 0.f, uu);
+      load_items<TI, K>(drow, t0, L, !MASKED, 0.f, dl);
+      load_items<TI, K>(dorow, t0, L, !MASKED, 0.f, dO);
+      if constexpr (HAS_Z) load_items<TI, K>(zrow, t0, L, !MASKED, 0.f, zz);
+    }
 #pragma unroll
     for (int i = 0; i < K; ++i) {
       const float raw = dl[i] + bias;
@@ -319,6 +373,7 @@ __device__ __forceinline__ void bwd_chunk(const BwdArgs& a, BwdSmem<TW, kBwdWarp
     }
     tmem_st2(tcar + kColDA + n0, dAc[0], dAc[1]);
   }
+  if (k > 0) load_chunk_items<TI, K, HAS_Z>(items, urow, drow, dorow, zrow, t0 - kChunk, L, next_vec);
   // -- sum the chunk's partials over the warps of the CTA. red is rewritten only in the next
   //    chunk, after the cluster barrier below, which every thread reaches after this sum.
   __syncthreads();
@@ -518,30 +573,37 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3) scan_bwd_kernel(const BwdAr
   const bool vec_io = f.vec_io != 0;
   const int nfull = (vec_io && staged) ? (int)(L / kChunk) : 0;
 
+  ChunkItems<TI, K> items;
+  if (f.nchunks > 0)
+    load_chunk_items<TI, K, HAS_Z>(items, urow, drow, dorow, zrow, (int64_t)(f.nchunks - 1) * kChunk + s * K, L,
+                                   f.nchunks - 1 < nfull);
   // The partial last chunk (and every chunk of an unaligned row) goes first: masked, direct loads.
   for (int k = f.nchunks - 1; k >= nfull; --k) {
     bwd_chunk<TI, TW, S, HAS_Z, false, true>(a, sm, 0, k, row, slice, cluster_idx, cl_c, valid, lane, warp, c, s,
                                              Bbase, Cbase, Dv, bias, urow, drow, dorow, zrow, dDacc, dbacc, rbuf,
-                                             tcar, cluster);
+                                             tcar, items, k - 1 < nfull, cluster);
   }
   // Full chunks, last to first: B/C + restart states staged one chunk ahead by the bulk-copy
-  // engine; the lane's own rows of the next chunk are prefetched into L2.
+  // engine; the lane's own items of the next chunk are loaded at the end of the current one (2-byte
+  // items) or prefetched into L2 (4-byte items).
   if (nfull > 0 && warp == 0) issue(nfull - 1, (nfull - 1) & 1);
   for (int k = nfull - 1; k >= 0; --k) {
     const int buf = k & 1;
     if (k > 0) {
-      const int64_t t1 = (int64_t)(k - 1) * kChunk + s * K;
-      prefetch_l2(urow + t1);
-      prefetch_l2(drow + t1);
-      prefetch_l2(dorow + t1);
-      if constexpr (HAS_Z) prefetch_l2(zrow + t1);
+      if constexpr (!ChunkItems<TI, K>::kCarry) {
+        const int64_t t1 = (int64_t)(k - 1) * kChunk + s * K;
+        prefetch_l2(urow + t1);
+        prefetch_l2(drow + t1);
+        prefetch_l2(dorow + t1);
+        if constexpr (HAS_Z) prefetch_l2(zrow + t1);
+      }
       if (warp == 0) issue(k - 1, buf ^ 1);
     }
     // Uses of bar[buf], from the last chunk downwards: chunk k is use number (nfull-1-k)/2.
     mbar_wait(&sm.bar[buf], (uint32_t)(((nfull - 1 - k) >> 1) & 1));
     bwd_chunk<TI, TW, S, HAS_Z, true, false>(a, sm, buf, k, row, slice, cluster_idx, cl_c, valid, lane, warp, c, s,
                                              Bbase, Cbase, Dv, bias, urow, drow, dorow, zrow, dDacc, dbacc, rbuf,
-                                             tcar, cluster);
+                                             tcar, items, true, cluster);
     // bwd_chunk ends with cluster.sync() after its last shared-memory read of this buffer, so the
     // next iteration may refill it.
   }
