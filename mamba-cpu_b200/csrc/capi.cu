@@ -86,7 +86,7 @@ BwdLayout bwd_layout(const ScanArgs& f, bool need_states, bool batch_partials) {
   const int S = bwd_segments(f.batch * f.dim);
   const int64_t cpc = kBwdWarps * (32 / S);
   const int64_t tiles = (f.dpg + cpc - 1) / cpc;
-  w.cluster = bwd_cluster_size(tiles);
+  w.cluster = bwd_cluster_size(tiles, f.batch * f.ngroups);
   w.clusters = (tiles + w.cluster - 1) / w.cluster;
   w.Lpad = (int64_t)f.nchunks * kChunk;
   const int64_t rows = f.batch * f.dim;

@@ -57,7 +57,7 @@ int fwd_states_per_lane(int64_t rows);
 cudaError_t read_fault_fwd(int* out);
 cudaError_t read_fault_bwd(int* out);
 int bwd_segments(int64_t rows);
-int bwd_cluster_size(int64_t tiles);
+int bwd_cluster_size(int64_t tiles, int64_t slices);
 
 cudaError_t launch_scan_fwd(const ScanArgs& a, int io_dtype, int bc_dtype, bool write_out,
                             cudaStream_t stream);

@@ -740,11 +740,25 @@ int bwd_segments(int64_t rows) { return rows >= 4096 ? 8 : 16; }
 
 cudaError_t read_fault_bwd(int* out) { return read_fault_word(out); }
 
-int bwd_cluster_size(int64_t tiles) {
-  if (tiles >= 8) return 8;
-  if (tiles >= 4) return 4;
-  if (tiles >= 2) return 2;
-  return 1;
+int bwd_cluster_size(int64_t tiles, int64_t slices) {
+  // Larger clusters divide the dB/dC partials written per slice (fewer cluster partials for the
+  // reduce kernel) but constrain where CTAs may be placed. When the grid fits one wave of
+  // resident CTAs (3 per SM), 8 is best; when it takes several waves, clusters of 8 leave SMs
+  // idle at the wave boundaries and pairs are faster (measured: BASELINE config 2 vs config 5).
+  static int sms = 0;
+  if (sms == 0) {
+    int dev = 0, n = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess && cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) ==
+                                                    cudaSuccess && n > 0)
+      sms = n;
+    else
+      sms = 148;
+  }
+  const int64_t ctas = tiles * slices;
+  const int cap = ctas <= (int64_t)sms * 3 ? 8 : 2;
+  int cl = 1;
+  while (cl * 2 <= cap && tiles >= cl * 2) cl *= 2;
+  return cl;
 }
 
 cudaError_t launch_scan_bwd(const BwdArgs& a, int io_dtype, int bc_dtype, int cluster, cudaStream_t stream) {
