@@ -188,6 +188,23 @@ __device__ __forceinline__ float softplus_f(float x) {
   return x <= 20.f ? r : x;  // NaN takes the first branch and stays NaN
 }
 
+// softplus_f(x) and its derivative sigmoid(x) from one exponential: with y = e^-|x|,
+// sigmoid(x) = (x >= 0 ? 1 : y) / (1 + y).
+__device__ __forceinline__ float softplus_dsig(float x, float& sig) {
+  const float y = __expf(-fabsf(x));
+  sig = __fdividef(x >= 0.f ? 1.f : y, 1.f + y);
+  const float s = __fdividef(y, 2.f + y);
+  const float s2 = s * s;
+  float p = fmaf(s2, 1.f / 13.f, 1.f / 11.f);
+  p = fmaf(s2, p, 1.f / 9.f);
+  p = fmaf(s2, p, 1.f / 7.f);
+  p = fmaf(s2, p, 1.f / 5.f);
+  p = fmaf(s2, p, 1.f / 3.f);
+  p = fmaf(s2, p, 1.f);
+  const float r = fmaxf(x, 0.f) + 2.f * s * p;
+  return x <= 20.f ? r : x;
+}
+
 // 1 / (1 + e^-x); +-inf inputs give 0 / 1 (the fast division returns 0 for denominators past
 // 2^126, the correctly rounded value to within its error bound).
 __device__ __forceinline__ float sigmoid_f(float x) { return __fdividef(1.f, 1.f + __expf(-x)); }

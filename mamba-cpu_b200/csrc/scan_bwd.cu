@@ -45,10 +45,12 @@ constexpr int kRedFloats = kMaxState * 2 * kChunk;  // one CTA's dB|dC chunk par
 
 constexpr int ilog2(int v) { return v <= 1 ? 0 : 1 + ilog2(v / 2); }
 
-// TMEM columns per CTA: per thread, the adjoint gh entering the current chunk (columns 0..15)
-// and the dA partial of each state (16..31).
-constexpr uint32_t kTmemCols = 32;
+// TMEM columns per CTA: per thread, the adjoint gh entering the current chunk (columns 0..15),
+// the dA partial of each state (16..31), and the chunk's u, softplus' and dz factor items
+// (32.., 3 x K columns) that the output stage reads back.
+constexpr uint32_t kTmemCols = 64;
 constexpr int kColDA = kMaxState;
+constexpr int kColItems = 2 * kMaxState;
 
 template <typename TW, int CPC>
 struct BwdSmem {
@@ -140,23 +142,34 @@ __device__ __forceinline__ void bwd_chunk(const BwdArgs& a, BwdSmem<TW, kBwdWarp
       load_items<TI, K>(dorow, t0, L, !MASKED, 0.f, dO);
       if constexpr (HAS_Z) load_items<TI, K>(zrow, t0, L, !MASKED, 0.f, zz);
     }
+    float dsp[K], dzf[K];  // softplus'(delta + bias); dout * silu'(z)
 #pragma unroll
     for (int i = 0; i < K; ++i) {
       const float raw = dl[i] + bias;
-      float dti = f.softplus ? softplus_f(raw) : raw;
+      float dti = raw;
+      dsp[i] = 1.f;
+      if (f.softplus) dti = softplus_dsig(raw, dsp[i]);
       if (MASKED) dti = (t0 + i < L) ? dti : 0.f;
       dt[i] = dti;
       dtu[i] = dti * uu[i];
       sdt += dti;
       float dyi = dO[i];
+      dzf[i] = 0.f;
       if constexpr (HAS_Z) {
-        dyi = dO[i] * zz[i] * sigmoid_f(zz[i]);
+        const float zs = sigmoid_f(zz[i]);
+        dyi = dO[i] * zz[i] * zs;
+        dzf[i] = dO[i] * zs * (1.f + zz[i] * (1.f - zs));
         y[i] = Dv * uu[i];
       }
       dy[i] = valid ? dyi : 0.f;
       gB[i] = 0.f;
       xA[i] = 0.f;
     }
+    // park the items the output stage needs in TMEM (the pair loop's first wait::st completes
+    // these stores)
+    tmem_st_n<K>(tcar + kColItems, uu);
+    tmem_st_n<K>(tcar + kColItems + K, dsp);
+    if constexpr (HAS_Z) tmem_st_n<K>(tcar + kColItems + 2 * K, dzf);
   }
 
   const TW* tB = &sm.bc[buf][0][0][0];
@@ -422,18 +435,15 @@ __device__ __forceinline__ void bwd_chunk(const BwdArgs& a, BwdSmem<TW, kBwdWarp
   rbuf ^= 1;
 
   // -- per-timestep gradients of this lane's K steps
-  float uu[K], dl[K], dO[K], zz[K];
-  load_items<TI, K>(urow, t0, L, !MASKED, 0.f, uu);
-  load_items<TI, K>(drow, t0, L, !MASKED, 0.f, dl);
-  if constexpr (HAS_Z) {
-    load_items<TI, K>(dorow, t0, L, !MASKED, 0.f, dO);
-    load_items<TI, K>(zrow, t0, L, !MASKED, 0.f, zz);
-  }
+  float uu[K], dsp[K], dzf[K];
+  tmem_ld_n<K>(tcar + kColItems, uu);
+  tmem_ld_n<K>(tcar + kColItems + K, dsp);
+  if constexpr (HAS_Z) tmem_ld_n<K>(tcar + kColItems + 2 * K, dzf);
+  tmem_wait_ld();
   float du[K], dd[K];
 #pragma unroll
   for (int i = 0; i < K; ++i) {
-    const float dsp = f.softplus ? sigmoid_f(dl[i] + bias) : 1.f;
-    const float ddt = (xA[i] + uu[i] * gB[i]) * dsp;
+    const float ddt = (xA[i] + uu[i] * gB[i]) * dsp[i];
     du[i] = Dv * dy[i] + dt[i] * gB[i];
     dd[i] = ddt;
     if (!MASKED || t0 + i < L) {
@@ -453,10 +463,7 @@ __device__ __forceinline__ void bwd_chunk(const BwdArgs& a, BwdSmem<TW, kBwdWarp
     }
     if constexpr (HAS_Z) {
 #pragma unroll
-      for (int i = 0; i < K; ++i) {
-        const float zs = sigmoid_f(zz[i]);
-        dd[i] = dO[i] * zs * (1.f + zz[i] * (1.f - zs)) * y[i];
-      }
+      for (int i = 0; i < K; ++i) dd[i] = dzf[i] * y[i];
       TI* dzrow = static_cast<TI*>(a.dz) + row * L;
       if (MASKED)
         store_items<TI, K>(dzrow, t0, L, false, dd);

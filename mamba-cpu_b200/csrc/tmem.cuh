@@ -56,6 +56,35 @@ __device__ __forceinline__ void tmem_st2(uint32_t taddr, float a, float b) {
                : "memory");
 }
 
+__device__ __forceinline__ void tmem_st4(uint32_t taddr, const float* v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(taddr),
+               "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+               "r"(__float_as_uint(v[3]))
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld4(uint32_t taddr, float* v) {
+  uint32_t r[4];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(taddr)
+               : "memory");
+#pragma unroll
+  for (int i = 0; i < 4; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// K consecutive columns (K a multiple of 4) from / to v[0..K).
+template <int K>
+__device__ __forceinline__ void tmem_st_n(uint32_t taddr, const float (&v)[K]) {
+#pragma unroll
+  for (int i = 0; i < K; i += 4) tmem_st4(taddr + i, v + i);
+}
+template <int K>
+__device__ __forceinline__ void tmem_ld_n(uint32_t taddr, float (&v)[K]) {
+#pragma unroll
+  for (int i = 0; i < K; i += 4) tmem_ld4(taddr + i, v + i);
+}
+
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   uint32_t r[16];
   asm volatile(
