@@ -6,8 +6,9 @@
 One step = one forward + backward selective scan over one batch of the configuration (default
 fp32, batch 4, dim 1536, seqlen 1024, dstate 16, z, delta_bias, softplus).
 With N GPUs every rank owns a 1536-channel shard of a dim = 1536*N problem (weak scaling): the
-forward needs no communication and the backward all-reduces the fp32 [dB | dC] partial sums with
-NCCL. Inputs are resident in HBM when the timed region starts; L2 (126 MB) is flushed with a
+forward needs no communication and the backward sums the fp32 [dB | dC] partial sums over the ranks
+in one exchange: a one-kernel sum read from the other GPUs' memory over NVLink (parallel.PeerReducer;
+MAMBA_B200_PEER_REDUCE=0 selects one NCCL all_reduce instead). Inputs are resident in HBM when the timed region starts; L2 (126 MB) is flushed with a
 256 MiB write before the forward and before the backward of every step. Kernel time is taken with
 CUDA events on the launching stream (max over ranks); the step's kernels are replayed from CUDA
 graphs so host launch latency is not measured.
@@ -364,6 +365,8 @@ def run_ours(args):
             "batch": b, "dim_per_rank": d, "seqlen": l, "dstate": n, "global_dim": d * world,
             "l2": "flushed (256 MiB write) before the forward and before the backward of every step",
             "parallelism": f"dim-shard{world}" if world > 1 else "single",
+            **({"dB_dC_exchange": "peer-memory one-shot sum (NVLink)"
+                if os.environ.get("MAMBA_B200_PEER_REDUCE", "1") != "0" else "NCCL all_reduce"} if world > 1 else {}),
         },
         "tokens_per_s": b * l / (ms_step * 1e-3),
         "ms_fwd": ms_fwd,

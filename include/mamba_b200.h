@@ -274,6 +274,39 @@ MB200_API int mb200_causal_conv1d_update(const mb200_conv1d_update_params* p, vo
 
 /* ---- misc -------------------------------------------------------------------------------- */
 
+/* ---- one-shot sum over the GPUs of a node through peer memory ------------------------------
+ *
+ * The dB / dC partial sums of a channel-sharded backward are combined across ranks by reading
+ * every rank's partial over NVLink instead of a ring all-reduce (which at these sizes, ~0.5 MB,
+ * is dominated by per-step latency). Every rank owns an exchange buffer of 2 * n floats (two
+ * slots, used alternately) and a signal pad of `world` uint32, shared with the other ranks of
+ * the node through CUDA IPC (plain peer mappings, no multicast objects):
+ *
+ *   mb200_peer_alloc                      zeroed device allocation (its own base, as IPC needs)
+ *   mb200_ipc_handle / mb200_ipc_open     export / map an allocation of another process
+ *   mb200_peer_sum_f32                    in place: a[0..na) | b[0..nb) := the sum over all ranks
+ *                                         of their a | b (every rank gets the same bits: ranks
+ *                                         are added in rank order)
+ *
+ * peer_bufs / peer_pads are DEVICE arrays of `world` pointers (this rank's own at index `rank`) to
+ * the ranks' exchange buffers (8 * ceil((na + nb) / 4) floats each) and signal pads (world *
+ * MB200_PEER_BLOCKS uint32 each, zeroed); `counters` is this rank's device array of
+ * MB200_PEER_BLOCKS uint32, zeroed, that only these calls advance (call numbers: they select the
+ * slot and the values the signals carry, so the call is valid inside CUDA graphs). One kernel of
+ * MB200_PEER_BLOCKS CTAs per call; CTA j of a rank waits only for CTA j of the others. The wait
+ * is bounded (~2 s); on timeout the fault word of mb200_device_fault gets bit 1 and the sums are
+ * unspecified. All ranks must make the same sequence of calls with the same sizes, and the
+ * calls of one rank on one set of buffers must not overlap (issue them on one stream).
+ */
+#define MB200_IPC_HANDLE_BYTES 64
+#define MB200_PEER_BLOCKS 148
+MB200_API int mb200_peer_alloc(size_t bytes, void** dev_ptr);
+MB200_API int mb200_ipc_handle(void* dev_ptr, unsigned char handle[MB200_IPC_HANDLE_BYTES]);
+MB200_API int mb200_ipc_open(const unsigned char handle[MB200_IPC_HANDLE_BYTES], void** dev_ptr);
+MB200_API int mb200_ipc_close(void* dev_ptr);
+MB200_API int mb200_peer_sum_f32(float* a, int64_t na, float* b, int64_t nb, float* const* peer_bufs,
+                                 uint32_t* const* peer_pads, uint32_t* counters, int rank, int world, void* stream);
+
 /* Static description of a status code. */
 MB200_API const char* mb200_status_string(int status);
 
@@ -285,7 +318,8 @@ MB200_API int mb200_last_launch_count(void);
 
 /* Read and clear the device-side fault word of the current device (synchronises the device).
  * Kernels never trap: a bounded wait that gave up (a staged copy that did not arrive in ~2.5 s)
- * sets bit 0 and the kernel finishes with unspecified outputs. *fault = 0 means no fault. */
+ * sets bit 0, a peer that did not signal within ~2 s (mb200_peer_sum_f32) bit 1, and the kernel
+ * finishes with unspecified outputs. *fault = 0 means no fault. */
 MB200_API int mb200_device_fault(int* fault);
 
 #ifdef __cplusplus

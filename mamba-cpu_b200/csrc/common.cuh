@@ -218,7 +218,7 @@ inline int dtype_size(int code) {
   return code == MB200_F32 ? 4 : (code == MB200_BF16 || code == MB200_F16) ? 2 : 0;
 }
 
-inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+__host__ __device__ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 // Kernel launch counter (per host thread) reported by mb200_last_launch_count().
 void note_launches(int n);

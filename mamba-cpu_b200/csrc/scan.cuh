@@ -56,6 +56,7 @@ int fwd_states_per_lane(int64_t rows);
 // Read and clear the device fault word of the forward / backward kernels (synchronous).
 cudaError_t read_fault_fwd(int* out);
 cudaError_t read_fault_bwd(int* out);
+cudaError_t read_fault_peer(int* out);
 int bwd_segments(int64_t rows);
 int bwd_cluster_size(int64_t tiles, int64_t slices);
 

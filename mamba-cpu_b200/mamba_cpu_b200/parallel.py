@@ -97,10 +97,103 @@ def new_reduce_group(dim: int, ngroups: int, rank: int, world: int):
     return mine
 
 
-def all_reduce_bc(dB: torch.Tensor, dC: torch.Tensor, group, async_op: bool = False):
-    """Sum the fp32 partial dB / dC over the shards of ``group`` with ONE collective."""
+PEER_BLOCKS = 148  # MB200_PEER_BLOCKS: CTAs of one mb200_peer_sum_f32 call
+
+
+class PeerReducer:
+    """One-shot sum of a pair of fp32 buffers (``na`` + ``nb`` elements) over the ranks of a
+    node-local group, read directly from every rank's memory over NVLink
+    (``mb200_peer_sum_f32``).
+
+    Each rank allocates an exchange buffer (two slots of na + nb floats, rounded up to a multiple
+    of 4) and a signal pad, exports
+    them with CUDA IPC and maps the other ranks' (all ranks construct the reducer together: it is
+    a collective). A call is one kernel launch on the current stream and no host work, so it can
+    be captured in a CUDA graph; every rank receives the same bits (ranks are added in rank
+    order). The mappings live until the process exits.
+    """
+
+    def __init__(self, na: int, nb: int, group):
+        import ctypes
+
+        import torch.distributed as dist
+
+        from . import _lib
+
+        self.na, self.nb = int(na), int(nb)
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        own, pad = ctypes.c_void_p(), ctypes.c_void_p()
+        _lib.check(_lib.lib.mb200_peer_alloc(2 * 16 * ((self.na + self.nb + 3) // 4), ctypes.byref(own)), "mb200_peer_alloc")
+        _lib.check(_lib.lib.mb200_peer_alloc(self.world * PEER_BLOCKS * 4, ctypes.byref(pad)), "mb200_peer_alloc")
+        handles = []
+        for p in (own, pad):
+            h = (ctypes.c_ubyte * 64)()
+            _lib.check(_lib.lib.mb200_ipc_handle(p, h), "mb200_ipc_handle")
+            handles.append(bytes(h))
+        everyone = [None] * self.world
+        dist.all_gather_object(everyone, handles, group=group)
+        bufs, pads = [], []
+        for q, (hb, hp) in enumerate(everyone):
+            if q == self.rank:
+                bufs.append(own.value)
+                pads.append(pad.value)
+                continue
+            for h, dst in ((hb, bufs), (hp, pads)):
+                mapped = ctypes.c_void_p()
+                _lib.check(_lib.lib.mb200_ipc_open((ctypes.c_ubyte * 64).from_buffer_copy(h), ctypes.byref(mapped)),
+                           "mb200_ipc_open")
+                dst.append(mapped.value)
+        self.dev_bufs = torch.tensor(bufs, dtype=torch.int64, device="cuda")
+        self.dev_pads = torch.tensor(pads, dtype=torch.int64, device="cuda")
+        self.counters = torch.zeros(PEER_BLOCKS, dtype=torch.int32, device="cuda")
+        torch.cuda.synchronize()
+        dist.barrier(group=group)  # every rank has mapped every buffer before anyone signals
+
+    def all_reduce_(self, a: torch.Tensor, b: torch.Tensor):
+        """Sum ``a`` and ``b`` (contiguous fp32 of the sizes given at construction) in place."""
+        from . import _lib
+
+        for t, n in ((a, self.na), (b, self.nb)):
+            assert t.dtype == torch.float32 and t.is_contiguous() and t.numel() == n
+        st = _lib.lib.mb200_peer_sum_f32(a.data_ptr(), self.na, b.data_ptr(), self.nb, self.dev_bufs.data_ptr(),
+                                         self.dev_pads.data_ptr(), self.counters.data_ptr(), self.rank, self.world,
+                                         _lib.stream_of(a))
+        _lib.check(st, "mb200_peer_sum_f32")
+        return a, b
+
+
+_reducers: dict = {}
+
+
+def _use_peer_sum(group, t: torch.Tensor) -> bool:
+    """Peer-memory sums need CUDA tensors, an NCCL group of ranks on one node, and are on unless
+    MAMBA_B200_PEER_REDUCE=0. Every rank evaluates the same conditions."""
+    import os
+
     import torch.distributed as dist
 
+    if not t.is_cuda or os.environ.get("MAMBA_B200_PEER_REDUCE", "1") == "0":
+        return False
+    if dist.get_backend(group) != "nccl":
+        return False
+    world = dist.get_world_size(group)
+    return world > 1 and int(os.environ.get("LOCAL_WORLD_SIZE", str(world))) >= world
+
+
+def all_reduce_bc(dB: torch.Tensor, dC: torch.Tensor, group, async_op: bool = False):
+    """Sum the fp32 partial dB / dC over the shards of ``group`` in ONE exchange and return the
+    sums. For node-local NCCL groups this is a one-shot sum over NVLink peer memory
+    (:class:`PeerReducer`) that overwrites dB and dC in place; otherwise one ``all_reduce`` of
+    their concatenation."""
+    import torch.distributed as dist
+
+    if (_use_peer_sum(group, dB) and dB.dtype == dC.dtype == torch.float32
+            and dB.is_contiguous() and dC.is_contiguous()):
+        key = (id(group), dB.numel(), dC.numel())
+        if key not in _reducers:
+            _reducers[key] = PeerReducer(dB.numel(), dC.numel(), group)
+        return _reducers[key].all_reduce_(dB, dC)
     flat = torch.cat([dB.reshape(-1), dC.reshape(-1)])
     work = dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=group, async_op=async_op)
     if async_op:

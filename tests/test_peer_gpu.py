@@ -1,0 +1,109 @@
+"""One-shot dB/dC sum over NVLink peer memory (parallel.PeerReducer, mb200_peer_sum_f32).
+
+Runs when the process sees at least 2 GPUs: 2 (and, with 4 GPUs visible, 4) NCCL ranks compare
+the peer-memory sum with the rank-ordered fp32 sum of all ranks' inputs (all-gathered; the kernel
+adds ranks in rank order, so the bits must agree) over several calls (both exchange slots; sizes that are not multiples of 4; a source
+that is 16-byte aligned on one rank and not on the other), inside a captured CUDA graph, and
+check the kernels' fault word (no wait timed out).
+"""
+
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_ordered_sum(dB, dC, group, world):
+    import torch.distributed as dist
+
+    flat = torch.cat([dB.reshape(-1), dC.reshape(-1)])
+    parts = [torch.empty_like(flat) for _ in range(world)]
+    dist.all_gather(parts, flat, group=group)
+    want = parts[0].clone()
+    for p in parts[1:]:
+        want += p
+    return want
+
+
+def _worker(rank, world, port, outdir):
+    import torch.distributed as dist
+
+    from mamba_cpu_b200 import _lib, parallel
+
+    torch.cuda.set_device(rank)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    os.environ["LOCAL_WORLD_SIZE"] = str(world)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
+    try:
+        group = dist.group.WORLD
+        results = {}
+        for size in (1003, 64 * 1024 + 1):
+            for it in range(5):  # alternates the two exchange slots
+                g = torch.Generator().manual_seed(100 * it + rank + size)
+                dB = torch.randn(2, 1, 4, size // 16, generator=g).cuda()
+                dC = torch.randn(size - dB.numel(), generator=g).cuda()
+                want = _rank_ordered_sum(dB, dC, group, world)
+                got_b, got_c = parallel.all_reduce_bc(dB, dC, group)
+                got = torch.cat([got_b.reshape(-1), got_c.reshape(-1)])
+                results[f"eq_{size}_{it}"] = bool(torch.equal(got, want))
+        # float4-sized pieces; odd ranks' dB starts 4 bytes into its storage, so the ranks access
+        # their sources differently (vector / scalar) while exchanging the same slot layout
+        for it in range(3):
+            g = torch.Generator().manual_seed(31 + it + rank)
+            dB = torch.randn(2 * 4 * 256 + 1, generator=g).cuda()[rank % 2:rank % 2 + 2 * 4 * 256].view(2, 1, 4, 256)
+            dC = torch.randn(2, 1, 4, 256, generator=g).cuda()
+            want = _rank_ordered_sum(dB, dC, group, world)
+            got_b, got_c = parallel.all_reduce_bc(dB, dC, group)
+            results[f"eq_vec_{it}"] = bool(torch.equal(torch.cat([got_b.reshape(-1), got_c.reshape(-1)]), want))
+        # inside a CUDA graph: static input, replayed with new contents
+        dB = torch.zeros(2, 1, 4, 1003 // 16, device="cuda")
+        dC = torch.zeros(1003 - dB.numel(), device="cuda")
+        parallel.all_reduce_bc(dB, dC, group)  # reducer exists before capture
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s), torch.cuda.graph(graph):
+            out_b, out_c = parallel.all_reduce_bc(dB, dC, group)
+        torch.cuda.current_stream().wait_stream(s)
+        for it in range(3):
+            g = torch.Generator().manual_seed(7 + it + 10 * rank)
+            dB.copy_(torch.randn(dB.shape, generator=g))
+            dC.copy_(torch.randn(dC.shape, generator=g))
+            want = _rank_ordered_sum(dB, dC, group, world)
+            graph.replay()
+            torch.cuda.synchronize()
+            results[f"graph_{it}"] = bool(torch.equal(torch.cat([out_b.reshape(-1), out_c.reshape(-1)]), want))
+        del graph
+        results["fault"] = _lib.device_fault()
+        np.save(os.path.join(outdir, f"peer{rank}.npy"), results)
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.timeout(300)
+@pytest.mark.parametrize("world", [2, 4])
+def test_peer_sum_is_the_rank_ordered_sum(tmp_path, world):
+    import torch.multiprocessing as mp
+
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True,
+                       start_method="spawn")
+    for r in range(world):
+        res = np.load(tmp_path / f"peer{r}.npy", allow_pickle=True).item()
+        assert res.pop("fault") == 0, "a peer wait timed out"
+        bad = [k for k, v in res.items() if not v]
+        assert not bad, f"rank {r}: peer sum differs from the rank-ordered sum in {bad}"
