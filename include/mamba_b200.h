@@ -294,8 +294,9 @@ MB200_API int mb200_causal_conv1d_update(const mb200_conv1d_update_params* p, vo
  * MB200_PEER_BLOCKS uint32, zeroed, that only these calls advance (call numbers: they select the
  * slot and the values the signals carry, so the call is valid inside CUDA graphs). One kernel of
  * MB200_PEER_BLOCKS CTAs per call; CTA j of a rank waits only for CTA j of the others. The wait
- * is bounded (~2 s); on timeout the fault word of mb200_device_fault gets bit 1 and the sums are
- * unspecified. All ranks must make the same sequence of calls with the same sizes, and the
+ * for the other ranks is bounded by timeout_us of GPU time (<= 0: 30 s); on timeout the fault
+ * word of mb200_device_fault gets bit 1 and this call's sums are unspecified (a rank arriving
+ * later may get unspecified sums too; the calls after it are unaffected). All ranks must make the same sequence of calls with the same sizes, and the
  * calls of one rank on one set of buffers must not overlap (issue them on one stream).
  */
 #define MB200_IPC_HANDLE_BYTES 64
@@ -305,7 +306,8 @@ MB200_API int mb200_ipc_handle(void* dev_ptr, unsigned char handle[MB200_IPC_HAN
 MB200_API int mb200_ipc_open(const unsigned char handle[MB200_IPC_HANDLE_BYTES], void** dev_ptr);
 MB200_API int mb200_ipc_close(void* dev_ptr);
 MB200_API int mb200_peer_sum_f32(float* a, int64_t na, float* b, int64_t nb, float* const* peer_bufs,
-                                 uint32_t* const* peer_pads, uint32_t* counters, int rank, int world, void* stream);
+                                 uint32_t* const* peer_pads, uint32_t* counters, int rank, int world,
+                                 int64_t timeout_us, void* stream);
 
 /* Static description of a status code. */
 MB200_API const char* mb200_status_string(int status);
@@ -318,8 +320,8 @@ MB200_API int mb200_last_launch_count(void);
 
 /* Read and clear the device-side fault word of the current device (synchronises the device).
  * Kernels never trap: a bounded wait that gave up (a staged copy that did not arrive in ~2.5 s)
- * sets bit 0, a peer that did not signal within ~2 s (mb200_peer_sum_f32) bit 1, and the kernel
- * finishes with unspecified outputs. *fault = 0 means no fault. */
+ * sets bit 0, a peer that did not signal within the timeout (mb200_peer_sum_f32) bit 1, and the
+ * kernel finishes with unspecified outputs. *fault = 0 means no fault. */
 MB200_API int mb200_device_fault(int* fault);
 
 #ifdef __cplusplus

@@ -32,12 +32,19 @@ namespace {
 constexpr int kFaultPeerTimeout = 2;
 constexpr int kPeerThreads = 256;
 constexpr int kMaxUnrolledRanks = 8;
-constexpr long long kSpinLimit = 16ll << 20;  // x >= 100 ns sleep -> >= ~2 s
+constexpr int64_t kDefaultTimeoutUs = 30ll * 1000 * 1000;  // a rank may lag (e.g. checkpointing)
 
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   uint32_t v;
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
+}
+
+// Nanoseconds since an arbitrary origin (the GPU's global timer).
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
 }
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
@@ -117,7 +124,8 @@ __device__ __forceinline__ void exchange_pass(float* a, int64_t na, float* b, in
 
 __global__ void __launch_bounds__(kPeerThreads) peer_allreduce(float* a, int64_t na, float* b, int64_t nb,
                                                                float* const* bufs, uint32_t* const* pads,
-                                                               uint32_t* counters, int rank, int world) {
+                                                               uint32_t* counters, int rank, int world,
+                                                               uint64_t timeout_ns) {
   __shared__ uint32_t s_e;
   const int j = blockIdx.x;
   if (threadIdx.x == 0) {
@@ -134,9 +142,11 @@ __global__ void __launch_bounds__(kPeerThreads) peer_allreduce(float* a, int64_t
     __threadfence_system();  // the CTA's copies (ordered before by the barrier), then the signal
     st_release_sys(pads[threadIdx.x] + rank * MB200_PEER_BLOCKS + j, e);
     const uint32_t* word = pads[rank] + threadIdx.x * MB200_PEER_BLOCKS + j;
-    long long it = 0;
-    while ((int)(ld_acquire_sys(word) - e) < 0) {
-      if (++it > kSpinLimit) {
+    // Bounded wait: timeout_ns of global time, or (should the timer not advance) timeout_ns / 64
+    // polls, each of which takes far longer than 64 ns (a system-scope load and a sleep).
+    const uint64_t t0 = global_ns();
+    for (uint64_t it = 1; (int)(ld_acquire_sys(word) - e) < 0; ++it) {
+      if (((it & 255) == 0 && global_ns() - t0 > timeout_ns) || it > timeout_ns / 64) {
         atomicOr(&g_mb200_fault, kFaultPeerTimeout);
         break;
       }
@@ -187,7 +197,8 @@ MB200_API int mb200_ipc_close(void* dev_ptr) {
 }
 
 MB200_API int mb200_peer_sum_f32(float* a, int64_t na, float* b, int64_t nb, float* const* peer_bufs,
-                                 uint32_t* const* peer_pads, uint32_t* counters, int rank, int world, void* stream) {
+                                 uint32_t* const* peer_pads, uint32_t* counters, int rank, int world,
+                                 int64_t timeout_us, void* stream) {
   reset_launches();
   if ((a == nullptr && na > 0) || (b == nullptr && nb > 0) || peer_bufs == nullptr || peer_pads == nullptr ||
       counters == nullptr)
@@ -195,7 +206,8 @@ MB200_API int mb200_peer_sum_f32(float* a, int64_t na, float* b, int64_t nb, flo
   if (na < 0 || nb < 0 || world < 1 || world > kPeerThreads || rank < 0 || rank >= world) return MB200_ERR_BAD_SHAPE;
   if (na + nb == 0) return MB200_OK;
   peer_allreduce<<<MB200_PEER_BLOCKS, kPeerThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      a, na, b, nb, peer_bufs, peer_pads, counters, rank, world);
+      a, na, b, nb, peer_bufs, peer_pads, counters, rank, world,
+      static_cast<uint64_t>(timeout_us > 0 ? timeout_us : kDefaultTimeoutUs) * 1000ull);
   if (cudaGetLastError() != cudaSuccess) return MB200_ERR_CUDA;
   note_launches(1);
   return MB200_OK;

@@ -111,7 +111,8 @@ SIGNATURES = {
     "mb200_ipc_handle": ([_vp, ctypes.POINTER(ctypes.c_ubyte)], ctypes.c_int),
     "mb200_ipc_open": ([ctypes.POINTER(ctypes.c_ubyte), ctypes.POINTER(_vp)], ctypes.c_int),
     "mb200_ipc_close": ([_vp], ctypes.c_int),
-    "mb200_peer_sum_f32": ([_vp, _i64, _vp, _i64, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, _vp], ctypes.c_int),
+    "mb200_peer_sum_f32": ([_vp, _i64, _vp, _i64, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, _i64, _vp],
+                           ctypes.c_int),
 }
 
 

@@ -115,6 +115,7 @@ class PeerReducer:
 
     def __init__(self, na: int, nb: int, group):
         import ctypes
+        import os
 
         import torch.distributed as dist
 
@@ -147,6 +148,9 @@ class PeerReducer:
         self.dev_bufs = torch.tensor(bufs, dtype=torch.int64, device="cuda")
         self.dev_pads = torch.tensor(pads, dtype=torch.int64, device="cuda")
         self.counters = torch.zeros(PEER_BLOCKS, dtype=torch.int32, device="cuda")
+        # how long a rank's kernel waits for the others before flagging fault bit 1 (a straggler
+        # that checkpoints between steps must stay under it)
+        self.timeout_us = int(float(os.environ.get("MAMBA_B200_PEER_TIMEOUT_S", "30")) * 1e6)
         torch.cuda.synchronize()
         dist.barrier(group=group)  # every rank has mapped every buffer before anyone signals
 
@@ -158,7 +162,7 @@ class PeerReducer:
             assert t.dtype == torch.float32 and t.is_contiguous() and t.numel() == n
         st = _lib.lib.mb200_peer_sum_f32(a.data_ptr(), self.na, b.data_ptr(), self.nb, self.dev_bufs.data_ptr(),
                                          self.dev_pads.data_ptr(), self.counters.data_ptr(), self.rank, self.world,
-                                         _lib.stream_of(a))
+                                         self.timeout_us, _lib.stream_of(a))
         _lib.check(st, "mb200_peer_sum_f32")
         return a, b
 

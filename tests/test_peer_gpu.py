@@ -1,5 +1,10 @@
 """One-shot dB/dC sum over NVLink peer memory (parallel.PeerReducer, mb200_peer_sum_f32).
 
+On one GPU, this process plays both ranks of a 2-rank exchange through local buffers: with the
+other rank's signals already set the call returns the bitwise sum of the two slots and signals the
+other rank; with no signal the bounded wait runs out (short timeout) and sets fault bit 1 while
+the context stays usable.
+
 Runs when the process sees at least 2 GPUs: 2 (and, with 4 GPUs visible, 4) NCCL ranks compare
 the peer-memory sum with the rank-ordered fp32 sum of all ranks' inputs (all-gathered; the kernel
 adds ranks in rank order, so the bits must agree) over several calls (both exchange slots; sizes that are not multiples of 4; a source
@@ -34,6 +39,66 @@ def _rank_ordered_sum(dB, dC, group, world):
     for p in parts[1:]:
         want += p
     return want
+
+
+def _fake_exchange(na, nb):
+    """Exchange buffers, signal pads and call counters of a 2-rank exchange, both on this GPU."""
+    from mamba_cpu_b200.parallel import PEER_BLOCKS
+
+    nq = (na + nb + 3) // 4
+    bufs = [torch.zeros(2 * 4 * nq, device="cuda") for _ in range(2)]
+    pads = [torch.zeros(2 * PEER_BLOCKS, dtype=torch.int32, device="cuda") for _ in range(2)]
+    counters = torch.zeros(PEER_BLOCKS, dtype=torch.int32, device="cuda")
+    return bufs, pads, counters
+
+
+def _peer_sum_as_rank0(a, b, bufs, pads, counters, timeout_us):
+    from mamba_cpu_b200 import _lib
+
+    dev_bufs = torch.tensor([t.data_ptr() for t in bufs], dtype=torch.int64, device="cuda")
+    dev_pads = torch.tensor([t.data_ptr() for t in pads], dtype=torch.int64, device="cuda")
+    st = _lib.lib.mb200_peer_sum_f32(a.data_ptr(), a.numel(), b.data_ptr(), b.numel(), dev_bufs.data_ptr(),
+                                     dev_pads.data_ptr(), counters.data_ptr(), 0, 2, timeout_us, _lib.stream_of(a))
+    _lib.check(st, "mb200_peer_sum_f32")
+    torch.cuda.synchronize()
+
+
+@pytest.mark.parametrize("na,nb", [(4096, 4096), (1003, 518)])
+def test_peer_sum_one_gpu_two_fake_ranks(na, nb):
+    from mamba_cpu_b200 import _lib
+    from mamba_cpu_b200.parallel import PEER_BLOCKS
+
+    g = torch.Generator().manual_seed(na + nb)
+    a, b = torch.randn(na, generator=g).cuda(), torch.randn(nb, generator=g).cuda()
+    other = torch.randn(na + nb, generator=g).cuda()
+    bufs, pads, counters = _fake_exchange(na, nb)
+    nq = (na + nb + 3) // 4
+    bufs[1][4 * nq:4 * nq + na + nb] = other  # call 1 uses slot 1
+    pads[0][PEER_BLOCKS:] = 1  # rank 1 has signalled call 1 to rank 0 from every CTA
+    want = torch.cat([a, b]) + other
+    _peer_sum_as_rank0(a, b, bufs, pads, counters, 10**6)
+    assert _lib.device_fault() == 0
+    assert torch.equal(torch.cat([a, b]), want)
+    assert bool((pads[1][:PEER_BLOCKS] == 1).all()), "rank 0 did not signal rank 1 from every CTA"
+    assert bool((counters == 1).all())
+
+
+def test_peer_wait_times_out_and_flags_fault():
+    """Nothing sets the other rank's signal: the wait gives up after the timeout (0.1 s), records
+    fault bit 1, and the device stays usable."""
+    import time
+
+    from mamba_cpu_b200 import _lib
+
+    a, b = torch.ones(256, device="cuda"), torch.ones(256, device="cuda")
+    bufs, pads, counters = _fake_exchange(256, 256)
+    t0 = time.perf_counter()
+    _peer_sum_as_rank0(a, b, bufs, pads, counters, 100_000)
+    elapsed = time.perf_counter() - t0
+    assert _lib.device_fault() == 2
+    assert 0.02 < elapsed < 20.0
+    x = torch.arange(10, device="cuda", dtype=torch.float32)
+    assert float(x.sum()) == 45.0  # the context is still usable
 
 
 def _worker(rank, world, port, outdir):
