@@ -45,6 +45,17 @@ constexpr int kRedFloats = kMaxState * 2 * kChunk;  // one CTA's dB|dC chunk par
 
 constexpr int ilog2(int v) { return v <= 1 ? 0 : 1 + ilog2(v / 2); }
 
+constexpr int kMaxCluster = 8;  // bwd_cluster_size never returns more
+
+// Split cluster barrier: every thread of every CTA of the cluster arrives (its earlier shared
+// memory writes released to the cluster), and waits until all have arrived (acquire).
+__device__ __forceinline__ void cluster_arrive_release() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_acquire() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
 // TMEM columns per CTA: per thread, the adjoint gh entering the current chunk (columns 0..15),
 // the dA partial of each state (16..31), and the chunk's u, softplus' and dz factor items
 // (32.., 3 x K columns) that the output stage reads back.
@@ -406,71 +417,106 @@ __device__ __forceinline__ void bwd_chunk(const BwdArgs& a, BwdSmem<TW, kBwdWarp
     }
   }
 
-  // -- sum over the CTAs of the cluster
-  cluster.sync();
+  // -- the per-timestep gradients of this lane's K steps
+  auto output_stage = [&]() {
+    float uu[K], dsp[K], dzf[K];
+    tmem_ld_n<K>(tcar + kColItems, uu);
+    tmem_ld_n<K>(tcar + kColItems + K, dsp);
+    if constexpr (HAS_Z) tmem_ld_n<K>(tcar + kColItems + 2 * K, dzf);
+    tmem_wait_ld();
+    float du[K], dd[K];
+#pragma unroll
+    for (int i = 0; i < K; ++i) {
+      const float ddt = (xA[i] + uu[i] * gB[i]) * dsp[i];
+      du[i] = Dv * dy[i] + dt[i] * gB[i];
+      dd[i] = ddt;
+      if (!MASKED || t0 + i < L) {
+        dbacc += ddt;
+        dDacc += dy[i] * uu[i];
+      }
+    }
+    if (valid) {
+      TI* durow = static_cast<TI*>(a.du) + row * L;
+      TI* ddrow = static_cast<TI*>(a.ddelta) + row * L;
+      if (MASKED) {
+        store_items<TI, K>(durow, t0, L, false, du);
+        store_items<TI, K>(ddrow, t0, L, false, dd);
+      } else {
+        store_stream<TI, K>(durow + t0, du);
+        store_stream<TI, K>(ddrow + t0, dd);
+      }
+      if constexpr (HAS_Z) {
+#pragma unroll
+        for (int i = 0; i < K; ++i) dd[i] = dzf[i] * y[i];
+        TI* dzrow = static_cast<TI*>(a.dz) + row * L;
+        if (MASKED)
+          store_items<TI, K>(dzrow, t0, L, false, dd);
+        else
+          store_stream<TI, K>(dzrow + t0, dd);
+      }
+    }
+  };
+  // -- sum over the CTAs of the cluster. With 4-byte items: arrive once this CTA's sums are in
+  //    red_out, write the per-timestep gradients while the other CTAs catch up, then wait and
+  //    read theirs. With 2-byte items (next chunk's items held in registers) that order spills
+  //    (measured slower): full barrier, peer sums, then the gradients.
+  constexpr bool kOverlap = !ChunkItems<TI, K>::kCarry;
+  cluster_arrive_release();
+  if constexpr (kOverlap) output_stage();
+  cluster_wait_acquire();
   {
     const int CL = (int)cluster.num_blocks();
     const int crank = (int)cluster.block_rank();
     const int per = (total4 + CL - 1) / CL;
     const int lo = crank * per;
     const int hi = min(total4, lo + per);
-    for (int f4 = lo + threadIdx.x; f4 < hi; f4 += blockDim.x) {
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int r = 0; r < CL; ++r) {
-        const float4* peer = reinterpret_cast<const float4*>(cluster.map_shared_rank(sm.red_out[rbuf], r));
-        const float4 o = peer[f4];
-        acc.x += o.x;
-        acc.y += o.y;
-        acc.z += o.z;
-        acc.w += o.w;
-      }
-      const int nq = f4 / (kChunk / 4);  // n * 2 + q
+    auto dst_of = [&](int f4) {  // this slice's cluster partial of float4 f4 (n * 2 + q, t4)
+      const int nq = f4 / (kChunk / 4);
       const int t4 = f4 % (kChunk / 4);
       const int n = nq >> 1, q = nq & 1;
-      float* dst = a.part_bc + (((slice * a.clusters + cluster_idx) * 2 + q) * N + n) * a.Lpad +
-                   (int64_t)k * kChunk + t4 * 4;
-      *reinterpret_cast<float4*>(dst) = acc;
+      return a.part_bc + (((slice * a.clusters + cluster_idx) * 2 + q) * N + n) * a.Lpad + (int64_t)k * kChunk +
+             t4 * 4;
+    };
+    if constexpr (ChunkItems<TI, K>::kCarry) {
+      // 2-byte items: the next chunk's items are held in registers here, so one peer load at a
+      // time (more loads in flight spill)
+      for (int f4 = lo + threadIdx.x; f4 < hi; f4 += blockDim.x) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int r = 0; r < CL; ++r) {
+          const float4 o = reinterpret_cast<const float4*>(cluster.map_shared_rank(sm.red_out[rbuf], r))[f4];
+          acc.x += o.x;
+          acc.y += o.y;
+          acc.z += o.z;
+          acc.w += o.w;
+        }
+        *reinterpret_cast<float4*>(dst_of(f4)) = acc;
+      }
+    } else {
+      // Each thread sums one half (a float2) of a float4 over the peers, in rank order, with the
+      // loads of four peers in flight at a time (distributed shared memory round trips are long).
+      for (int h2 = 2 * lo + threadIdx.x; h2 < 2 * hi; h2 += blockDim.x) {
+        float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int r0 = 0; r0 < kMaxCluster; r0 += 4) {
+          float2 o[4];
+#pragma unroll
+          for (int r = 0; r < 4; ++r)
+            if (r0 + r < CL)
+              o[r] = reinterpret_cast<const float2*>(cluster.map_shared_rank(sm.red_out[rbuf], r0 + r))[h2];
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            if (r0 + r < CL) {
+              acc.x += o[r].x;
+              acc.y += o[r].y;
+            }
+          }
+        }
+        *reinterpret_cast<float2*>(dst_of(h2 >> 1) + (h2 & 1) * 2) = acc;
+      }
     }
   }
   rbuf ^= 1;
-
-  // -- per-timestep gradients of this lane's K steps
-  float uu[K], dsp[K], dzf[K];
-  tmem_ld_n<K>(tcar + kColItems, uu);
-  tmem_ld_n<K>(tcar + kColItems + K, dsp);
-  if constexpr (HAS_Z) tmem_ld_n<K>(tcar + kColItems + 2 * K, dzf);
-  tmem_wait_ld();
-  float du[K], dd[K];
-#pragma unroll
-  for (int i = 0; i < K; ++i) {
-    const float ddt = (xA[i] + uu[i] * gB[i]) * dsp[i];
-    du[i] = Dv * dy[i] + dt[i] * gB[i];
-    dd[i] = ddt;
-    if (!MASKED || t0 + i < L) {
-      dbacc += ddt;
-      dDacc += dy[i] * uu[i];
-    }
-  }
-  if (valid) {
-    TI* durow = static_cast<TI*>(a.du) + row * L;
-    TI* ddrow = static_cast<TI*>(a.ddelta) + row * L;
-    if (MASKED) {
-      store_items<TI, K>(durow, t0, L, false, du);
-      store_items<TI, K>(ddrow, t0, L, false, dd);
-    } else {
-      store_stream<TI, K>(durow + t0, du);
-      store_stream<TI, K>(ddrow + t0, dd);
-    }
-    if constexpr (HAS_Z) {
-#pragma unroll
-      for (int i = 0; i < K; ++i) dd[i] = dzf[i] * y[i];
-      TI* dzrow = static_cast<TI*>(a.dz) + row * L;
-      if (MASKED)
-        store_items<TI, K>(dzrow, t0, L, false, dd);
-      else
-        store_stream<TI, K>(dzrow + t0, dd);
-    }
-  }
+  if constexpr (!kOverlap) output_stage();
 }
 
 template <typename TI, typename TW, int S, bool HAS_Z>
@@ -611,8 +657,8 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3) scan_bwd_kernel(const BwdAr
     bwd_chunk<TI, TW, S, HAS_Z, true, false>(a, sm, buf, k, row, slice, cluster_idx, cl_c, valid, lane, warp, c, s,
                                              Bbase, Cbase, Dv, bias, urow, drow, dorow, zrow, dDacc, dbacc, rbuf,
                                              tcar, items, true, cluster);
-    // bwd_chunk ends with cluster.sync() after its last shared-memory read of this buffer, so the
-    // next iteration may refill it.
+    // bwd_chunk ends with a cluster barrier wait after its last shared-memory read of this
+    // buffer (and of red), so the next iteration may refill it.
   }
 
   // -- the adjoint entering the first step is the gradient of the initial state (every segment
@@ -709,7 +755,8 @@ __global__ void scan_bwd_reduce_kernel(const BwdArgs a, TO* dB, TO* dC, int64_t 
       const int64_t t = t4 * 4;
       if (t >= L) continue;
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int cl = 0; cl < a.clusters; ++cl) {
+#pragma unroll 4
+      for (int cl = 0; cl < a.clusters; ++cl) {  // unrolled: four loads in flight, adds in order
         const float4 o = *reinterpret_cast<const float4*>(
             a.part_bc + (((slice * a.clusters + cl) * 2 + q) * N + n) * Lpad + t);
         acc.x += o.x;
@@ -762,7 +809,7 @@ int bwd_cluster_size(int64_t tiles, int64_t slices) {
       sms = 148;
   }
   const int64_t ctas = tiles * slices;
-  const int cap = ctas <= (int64_t)sms * 3 ? 8 : 2;
+  const int cap = ctas <= (int64_t)sms * 3 ? kMaxCluster : 2;
   int cl = 1;
   while (cl * 2 <= cap && tiles >= cl * 2) cl *= 2;
   return cl;
