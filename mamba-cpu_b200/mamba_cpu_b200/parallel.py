@@ -122,6 +122,7 @@ class PeerReducer:
         from . import _lib
 
         self.na, self.nb = int(na), int(nb)
+        self.group = group  # held: the reducer cache is keyed by id(group), which must stay unique
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
         own, pad = ctypes.c_void_p(), ctypes.c_void_p()
