@@ -282,7 +282,7 @@ MB200_API int mb200_causal_conv1d_update(const mb200_conv1d_update_params* p, vo
  * slots, used alternately) and a signal pad of `world` uint32, shared with the other ranks of
  * the node through CUDA IPC (plain peer mappings, no multicast objects):
  *
- *   mb200_peer_alloc                      zeroed device allocation (its own base, as IPC needs)
+ *   mb200_peer_alloc / mb200_peer_free    zeroed device allocation (its own base, as IPC needs)
  *   mb200_ipc_handle / mb200_ipc_open     export / map an allocation of another process
  *   mb200_peer_sum_f32                    in place: a[0..na) | b[0..nb) := the sum over all ranks
  *                                         of their a | b (every rank gets the same bits: ranks
@@ -302,6 +302,7 @@ MB200_API int mb200_causal_conv1d_update(const mb200_conv1d_update_params* p, vo
 #define MB200_IPC_HANDLE_BYTES 64
 #define MB200_PEER_BLOCKS 148
 MB200_API int mb200_peer_alloc(size_t bytes, void** dev_ptr);
+MB200_API int mb200_peer_free(void* dev_ptr);
 MB200_API int mb200_ipc_handle(void* dev_ptr, unsigned char handle[MB200_IPC_HANDLE_BYTES]);
 MB200_API int mb200_ipc_open(const unsigned char handle[MB200_IPC_HANDLE_BYTES], void** dev_ptr);
 MB200_API int mb200_ipc_close(void* dev_ptr);

@@ -191,6 +191,11 @@ MB200_API int mb200_peer_alloc(size_t bytes, void** dev_ptr) {
   return MB200_OK;
 }
 
+MB200_API int mb200_peer_free(void* dev_ptr) {
+  if (dev_ptr == nullptr) return MB200_ERR_NULL_POINTER;
+  return cudaFree(dev_ptr) == cudaSuccess ? MB200_OK : MB200_ERR_CUDA;
+}
+
 MB200_API int mb200_ipc_close(void* dev_ptr) {
   if (dev_ptr == nullptr) return MB200_ERR_NULL_POINTER;
   return cudaIpcCloseMemHandle(dev_ptr) == cudaSuccess ? MB200_OK : MB200_ERR_CUDA;

@@ -108,6 +108,7 @@ SIGNATURES = {
     "mb200_last_launch_count": ([], ctypes.c_int),
     "mb200_device_fault": ([ctypes.POINTER(ctypes.c_int)], ctypes.c_int),
     "mb200_peer_alloc": ([ctypes.c_size_t, ctypes.POINTER(_vp)], ctypes.c_int),
+    "mb200_peer_free": ([_vp], ctypes.c_int),
     "mb200_ipc_handle": ([_vp, ctypes.POINTER(ctypes.c_ubyte)], ctypes.c_int),
     "mb200_ipc_open": ([ctypes.POINTER(ctypes.c_ubyte), ctypes.POINTER(_vp)], ctypes.c_int),
     "mb200_ipc_close": ([_vp], ctypes.c_int),

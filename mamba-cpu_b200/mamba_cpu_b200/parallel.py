@@ -106,54 +106,98 @@ class PeerReducer:
     (``mb200_peer_sum_f32``).
 
     Each rank allocates an exchange buffer (two slots of na + nb floats, rounded up to a multiple
-    of 4) and a signal pad, exports
-    them with CUDA IPC and maps the other ranks' (all ranks construct the reducer together: it is
-    a collective). A call is one kernel launch on the current stream and no host work, so it can
-    be captured in a CUDA graph; every rank receives the same bits (ranks are added in rank
-    order). The mappings live until the process exits.
+    of 4) and a signal pad, exports them with CUDA IPC and maps the other ranks' (all ranks build
+    the reducer together with :meth:`create`, a collective). A call is one kernel launch on the
+    current stream and no host work, so it can be captured in a CUDA graph; every rank receives
+    the same bits (ranks are added in rank order). The buffers and mappings live until the
+    process exits.
     """
 
-    def __init__(self, na: int, nb: int, group):
-        import ctypes
+    def __init__(self, na: int, nb: int, group, bufs, pads, owned):
         import os
 
         import torch.distributed as dist
-
-        from . import _lib
 
         self.na, self.nb = int(na), int(nb)
         self.group = group  # held: the reducer cache is keyed by id(group), which must stay unique
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
-        own, pad = ctypes.c_void_p(), ctypes.c_void_p()
-        _lib.check(_lib.lib.mb200_peer_alloc(2 * 16 * ((self.na + self.nb + 3) // 4), ctypes.byref(own)), "mb200_peer_alloc")
-        _lib.check(_lib.lib.mb200_peer_alloc(self.world * PEER_BLOCKS * 4, ctypes.byref(pad)), "mb200_peer_alloc")
-        handles = []
-        for p in (own, pad):
-            h = (ctypes.c_ubyte * 64)()
-            _lib.check(_lib.lib.mb200_ipc_handle(p, h), "mb200_ipc_handle")
-            handles.append(bytes(h))
-        everyone = [None] * self.world
-        dist.all_gather_object(everyone, handles, group=group)
-        bufs, pads = [], []
-        for q, (hb, hp) in enumerate(everyone):
-            if q == self.rank:
-                bufs.append(own.value)
-                pads.append(pad.value)
-                continue
-            for h, dst in ((hb, bufs), (hp, pads)):
-                mapped = ctypes.c_void_p()
-                _lib.check(_lib.lib.mb200_ipc_open((ctypes.c_ubyte * 64).from_buffer_copy(h), ctypes.byref(mapped)),
-                           "mb200_ipc_open")
-                dst.append(mapped.value)
+        self._owned = owned  # this rank's allocations and its mappings of the others'
         self.dev_bufs = torch.tensor(bufs, dtype=torch.int64, device="cuda")
         self.dev_pads = torch.tensor(pads, dtype=torch.int64, device="cuda")
         self.counters = torch.zeros(PEER_BLOCKS, dtype=torch.int32, device="cuda")
         # how long a rank's kernel waits for the others before flagging fault bit 1 (a straggler
         # that checkpoints between steps must stay under it)
         self.timeout_us = int(float(os.environ.get("MAMBA_B200_PEER_TIMEOUT_S", "30")) * 1e6)
+
+    @classmethod
+    def create(cls, na: int, nb: int, group):
+        """Build the reducer on every rank of ``group`` (a collective), or return None on every
+        rank when any rank could not allocate, export or map the buffers (no CUDA IPC between
+        the processes, for instance): the caller then uses NCCL. Every rank takes the same
+        collective steps whatever fails locally. Not allowed while a CUDA graph is captured."""
+        import ctypes
+
+        import torch.distributed as dist
+
+        from . import _lib
+
+        if torch.cuda.is_available() and torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("the dB/dC peer exchange is set up by the first sharded backward, which must run "
+                               "before CUDA graph capture")
+        rank, world = dist.get_rank(group), dist.get_world_size(group)
+        na, nb = int(na), int(nb)
+        owned = []  # (kind, pointer): "alloc" -> mb200_peer_free, "map" -> mb200_ipc_close
+
+        def release():
+            for kind, ptr in reversed(owned):
+                (_lib.lib.mb200_peer_free if kind == "alloc" else _lib.lib.mb200_ipc_close)(ptr)
+            owned.clear()
+
+        handles, err = None, ""
+        try:  # local: allocate and export
+            ptrs = []
+            for nbytes in (2 * 16 * ((na + nb + 3) // 4), world * PEER_BLOCKS * 4):
+                p = ctypes.c_void_p()
+                _lib.check(_lib.lib.mb200_peer_alloc(nbytes, ctypes.byref(p)), "mb200_peer_alloc")
+                owned.append(("alloc", p.value))
+                ptrs.append(p.value)
+            handles = []
+            for ptr in ptrs:
+                h = (ctypes.c_ubyte * 64)()
+                _lib.check(_lib.lib.mb200_ipc_handle(ctypes.c_void_p(ptr), h), "mb200_ipc_handle")
+                handles.append(bytes(h))
+        except (RuntimeError, ValueError, OSError) as e:
+            handles, err = None, str(e)
+        everyone = [None] * world
+        dist.all_gather_object(everyone, (handles, err), group=group)
+        bufs, pads = [], []
+        if all(h is not None for h, _ in everyone):
+            try:  # local: map the other ranks' buffers
+                for q, (hq, _) in enumerate(everyone):
+                    if q == rank:
+                        bufs.append(owned[0][1])
+                        pads.append(owned[1][1])
+                        continue
+                    for h, dst in zip(hq, (bufs, pads)):
+                        mapped = ctypes.c_void_p()
+                        _lib.check(_lib.lib.mb200_ipc_open((ctypes.c_ubyte * 64).from_buffer_copy(h),
+                                                           ctypes.byref(mapped)), "mb200_ipc_open")
+                        owned.append(("map", mapped.value))
+                        dst.append(mapped.value)
+            except (RuntimeError, ValueError, OSError) as e:
+                err = str(e)
+        else:
+            err = err or "another rank could not set up its exchange buffers"
+        oks = [None] * world
+        dist.all_gather_object(oks, err == "", group=group)
+        if not all(oks):
+            release()
+            return None
+        reducer = cls(na, nb, group, bufs, pads, owned)
         torch.cuda.synchronize()
         dist.barrier(group=group)  # every rank has mapped every buffer before anyone signals
+        return reducer
 
     def all_reduce_(self, a: torch.Tensor, b: torch.Tensor):
         """Sum ``a`` and ``b`` (contiguous fp32 of the sizes given at construction) in place."""
@@ -196,9 +240,11 @@ def all_reduce_bc(dB: torch.Tensor, dC: torch.Tensor, group, async_op: bool = Fa
     if (_use_peer_sum(group, dB) and dB.dtype == dC.dtype == torch.float32
             and dB.is_contiguous() and dC.is_contiguous()):
         key = (id(group), dB.numel(), dC.numel())
-        if key not in _reducers:
-            _reducers[key] = PeerReducer(dB.numel(), dC.numel(), group)
-        return _reducers[key].all_reduce_(dB, dC)
+        if key not in _reducers:  # None: the peer exchange is unavailable for this group (NCCL)
+            _reducers[key] = (group, PeerReducer.create(dB.numel(), dC.numel(), group))
+        reducer = _reducers[key][1]
+        if reducer is not None:
+            return reducer.all_reduce_(dB, dC)
     flat = torch.cat([dB.reshape(-1), dC.reshape(-1)])
     work = dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=group, async_op=async_op)
     if async_op:

@@ -264,3 +264,71 @@ def test_sequence_sharded_scan_equals_unsharded(tmp_path, world, L):
             np.testing.assert_allclose(p[k], want[key][..., lo:hi], rtol=1e-4, atol=1e-5, err_msg=k)
         for k, key in (("dA", "dA"), ("dD", "dD"), ("ddelta_bias", "ddelta_bias")):
             np.testing.assert_allclose(p[k], want[key], rtol=1e-4, atol=1e-5, err_msg=k)
+
+
+class _FakePeerLib:
+    """Stands in for libmamba_b200's peer entry points on CPU: hands out fake addresses, records
+    what is released, and fails the call named in ``fail`` (on the rank it is given to). Other
+    entry points (status strings) come from the real library."""
+
+    def __init__(self, fail, real):
+        self.fail = fail
+        self.real = real
+        self.live = set()
+        self.next = 0x1000
+
+    def __getattr__(self, name):
+        return getattr(self.real, name)
+
+    def _new(self, out):
+        self.next += 0x1000
+        out._obj.value = self.next
+        self.live.add(self.next)
+        return 0
+
+    def mb200_peer_alloc(self, nbytes, out):
+        return 7 if self.fail == "alloc" else self._new(out)
+
+    def mb200_ipc_handle(self, ptr, handle):
+        handle[0] = 1
+        return 0
+
+    def mb200_ipc_open(self, handle, out):
+        return 7 if self.fail == "open" else self._new(out)
+
+    def mb200_peer_free(self, ptr):
+        self.live.discard(int(ptr))
+        return 0
+
+    def mb200_ipc_close(self, ptr):
+        self.live.discard(int(ptr))
+        return 0
+
+
+def _peer_setup_worker(rank, port, fail_rank, fail, outdir):
+    import torch.distributed as dist
+
+    from mamba_cpu_b200 import _lib
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=WORLD)
+    try:
+        fake = _FakePeerLib(fail if rank == fail_rank else None, _lib.lib)
+        _lib.lib = fake
+        red = parallel.PeerReducer.create(1000, 24, dist.group.WORLD)
+        np.save(os.path.join(outdir, f"p{rank}.npy"), {"none": red is None, "leaked": len(fake.live)})
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.timeout(300)
+@pytest.mark.parametrize("fail", ["alloc", "open"])
+def test_peer_exchange_setup_failure_falls_back_on_every_rank(tmp_path, fail):
+    """One rank cannot allocate (or map) the exchange buffers: every rank gets None -- the NCCL
+    path -- instead of hanging in the set-up's collectives, and nothing set up stays allocated or
+    mapped."""
+    mp.start_processes(_peer_setup_worker, args=(_free_port(), 1, fail, str(tmp_path)), nprocs=WORLD, join=True,
+                       start_method="spawn")
+    for r in range(WORLD):
+        res = np.load(tmp_path / f"p{r}.npy", allow_pickle=True).item()
+        assert res["none"], f"rank {r} built a reducer although rank 1 failed"
+        assert res["leaked"] == 0, f"rank {r} kept {res['leaked']} buffers or mappings"
