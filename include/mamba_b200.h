@@ -61,7 +61,9 @@ extern "C" {
 
 /*
  * Forward scan parameters. Shapes (elements; all dense unless a stride is given):
- *   u, delta, z, out : (batch, dim, seqlen), dtype io_dtype, contiguous
+ *   u, delta, z      : (batch, dim, seqlen), dtype io_dtype; seqlen-contiguous rows, batch / dim
+ *                      strides below (dense by default)
+ *   out              : (batch, dim, seqlen), dtype io_dtype, contiguous
  *   A                : (dim, dstate) float32, contiguous
  *   B, C             : (batch, ngroups, dstate, seqlen), dtype bc_dtype, element strides given
  *                      below. seqlen stride 1 (the upstream layout) takes the vectorised path;
@@ -97,6 +99,15 @@ typedef struct mb200_scan_fwd_params {
   int32_t bc_dtype;
   int32_t delta_softplus;
   int32_t reserved;
+  /* Element strides of u, delta and z over batch and over dim; along seqlen they are contiguous.
+   * 0 selects the dense value (dim * seqlen, seqlen); negative strides are rejected
+   * (MB200_ERR_BAD_LAYOUT). Lets a caller hand over views -- the transposed delta projection,
+   * one half of the in_proj output as z -- without copying them. The vectorised path needs
+   * every row start 16-byte aligned; other strides run on the scalar-load path. The outputs and
+   * the backward's dout, du, ddelta, dz stay dense. */
+  int64_t u_batch_stride, u_dim_stride;
+  int64_t delta_batch_stride, delta_dim_stride;
+  int64_t z_batch_stride, z_dim_stride;
 } mb200_scan_fwd_params;
 
 /*

@@ -65,8 +65,22 @@ int build_scan_args(const mb200_scan_fwd_params* p, bool need_out, ScanArgs* a) 
   a->tiles = 0;
   a->nchunks = (int)((p->seqlen + kChunk - 1) / kChunk);
   a->softplus = p->delta_softplus != 0;
+  const int64_t dense_b = p->dim * p->seqlen, dense_d = p->seqlen;
+  auto pick = [](int64_t s, int64_t dense) { return s != 0 ? s : dense; };
+  a->sub = pick(p->u_batch_stride, dense_b);
+  a->sud = pick(p->u_dim_stride, dense_d);
+  a->sdb = pick(p->delta_batch_stride, dense_b);
+  a->sdd = pick(p->delta_dim_stride, dense_d);
+  a->szb = pick(p->z_batch_stride, dense_b);
+  a->szd = pick(p->z_dim_stride, dense_d);
+  const int64_t io_strides[6] = {a->sub, a->sud, a->sdb, a->sdd, a->szb, a->szd};
+  bool io_rows16 = true;
+  for (int64_t v : io_strides) {
+    if (v < 0) return MB200_ERR_BAD_LAYOUT;
+    io_rows16 = io_rows16 && (v * es) % 16 == 0;
+  }
   const bool io_al = aligned16(p->u) && aligned16(p->delta) && aligned16(p->z) && aligned16(p->out);
-  a->vec_io = io_al && ((p->seqlen * es) % 16 == 0);
+  a->vec_io = io_al && io_rows16 && ((p->seqlen * es) % 16 == 0);
   const bool bc_al = aligned16(p->B) && aligned16(p->C);
   auto row16 = [&](int64_t s) { return (s * bs) % 16 == 0; };
   a->vec_bc = bc_al && p->B_seqlen_stride == 1 && p->C_seqlen_stride == 1 && row16(p->B_batch_stride) &&
@@ -429,7 +443,7 @@ MB200_API const char* mb200_status_string(int status) {
   }
 }
 
-MB200_API int mb200_version(void) { return (1 << 16) | 1; }
+MB200_API int mb200_version(void) { return (1 << 16) | 2; }
 
 MB200_API int mb200_last_launch_count(void) { return g_launches; }
 

@@ -26,12 +26,22 @@ struct ScanArgs {
   const float* h_init;  // (batch, dim, dstate) state before the first step, or NULL (zeros)
   int64_t batch, dim, L, N, ngroups, dpg;
   int64_t sBb, sBg, sBn, sBl, sCb, sCg, sCn, sCl;
+  int64_t sub, sud, sdb, sdd, szb, szd;  // batch / dim element strides of u, delta, z
   int tiles;    // CTAs per (batch, group) slice
   int nchunks;  // ceil(L / kChunk)
   int softplus;
   int vec_io;   // u / delta / z / out rows allow 16-byte vector access
   int vec_bc;   // B / C are l-contiguous and aligned
 };
+
+// True when u, delta or z are not dense (batch, dim, seqlen) rows: the launchers then pick the
+// kernels' STRIDED instantiations, which address rows through the batch / dim strides. The dense
+// instantiations keep the plain row * seqlen addressing (and its register allocation).
+inline bool io_rows_strided(const ScanArgs& a) {
+  const int64_t db = a.dim * a.L, dd = a.L;
+  return a.sub != db || a.sud != dd || a.sdb != db || a.sdd != dd ||
+         (a.z != nullptr && (a.szb != db || a.szd != dd));
+}
 
 struct BwdArgs {
   ScanArgs f;

@@ -519,7 +519,7 @@ __device__ __forceinline__ void bwd_chunk(const BwdArgs& a, BwdSmem<TW, kBwdWarp
   if constexpr (!kOverlap) output_stage();
 }
 
-template <typename TI, typename TW, int S, bool HAS_Z>
+template <typename TI, typename TW, int S, bool HAS_Z, bool STRIDED>
 __global__ void __launch_bounds__(kBwdWarps * 32, 3) scan_bwd_kernel(const BwdArgs a) {
   constexpr int K = kChunk / S;
   constexpr int CW = 32 / S;
@@ -552,9 +552,11 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3) scan_bwd_kernel(const BwdAr
   const int N = (int)f.N;
   const int64_t nvalid = f.dpg - tile_c0 < CPC ? (f.dpg - tile_c0 > 0 ? f.dpg - tile_c0 : 0) : CPC;
 
-  const TI* urow = static_cast<const TI*>(f.u) + row * L;
-  const TI* drow = static_cast<const TI*>(f.delta) + row * L;
-  const TI* zrow = HAS_Z ? static_cast<const TI*>(f.z) + row * L : nullptr;
+  // u / delta / z rows: dense (row * L) or, in the STRIDED instantiations, strided views (batch
+  // and dim strides of their own); separate instantiations keep the dense kernels' registers.
+  const TI* urow = static_cast<const TI*>(f.u) + (STRIDED ? b * f.sub + d * f.sud : row * L);
+  const TI* drow = static_cast<const TI*>(f.delta) + (STRIDED ? b * f.sdb + d * f.sdd : row * L);
+  const TI* zrow = HAS_Z ? static_cast<const TI*>(f.z) + (STRIDED ? b * f.szb + d * f.szd : row * L) : nullptr;
   const TI* dorow = static_cast<const TI*>(a.dout) + row * L;
   const TW* Bbase = static_cast<const TW*>(f.B) + b * f.sBb + g * f.sBg;
   const TW* Cbase = static_cast<const TW*>(f.C) + b * f.sCb + g * f.sCg;
@@ -712,7 +714,9 @@ cudaError_t launch_typed(BwdArgs a, int cluster, cudaStream_t stream) {
   a.f.tiles = (int)(((tiles + cluster - 1) / cluster) * cluster);
   a.clusters = a.f.tiles / cluster;
   constexpr size_t smem = sizeof(BwdSmem<TW, CPC>);
-  auto kern = a.f.z != nullptr ? scan_bwd_kernel<TI, TW, S, true> : scan_bwd_kernel<TI, TW, S, false>;
+  const bool strided = io_rows_strided(a.f);
+  auto kern = a.f.z != nullptr ? (strided ? scan_bwd_kernel<TI, TW, S, true, true> : scan_bwd_kernel<TI, TW, S, true, false>)
+                               : (strided ? scan_bwd_kernel<TI, TW, S, false, true> : scan_bwd_kernel<TI, TW, S, false, false>);
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};

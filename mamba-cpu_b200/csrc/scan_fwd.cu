@@ -136,7 +136,7 @@ __device__ __forceinline__ void recur_chunk(FwdSmem<NS>& sm, int cl, int p, cons
   }
 }
 
-template <typename TI, typename TW, int NS, bool HAS_Z, bool WRITE_OUT>
+template <typename TI, typename TW, int NS, bool HAS_Z, bool WRITE_OUT, bool STRIDED>
 __global__ void __launch_bounds__(kThreads, 3) scan_fwd_kernel(const ScanArgs a) {
   using Sh = FwdShape<NS>;
   constexpr int kTasks = Sh::kTasks;
@@ -206,17 +206,20 @@ __global__ void __launch_bounds__(kThreads, 3) scan_fwd_kernel(const ScanArgs a)
     for (int i = 0; i < kTasks; ++i) {
       const int64_t t = t0 + 4 * tq[i];
       if (tc[i] < nvalid) {
+        // row (b, d0 + tc[i]) of u / delta / z: dense, or strided views in the STRIDED instantiations
+        const int64_t dch = d0 + tc[i];
         const int64_t off = (row0 + tc[i]) * L;
-        const TI* u = static_cast<const TI*>(a.u) + off;
-        const TI* dl = static_cast<const TI*>(a.delta) + off;
+        const TI* u = static_cast<const TI*>(a.u) + (STRIDED ? b * a.sub + dch * a.sud : off);
+        const TI* dl = static_cast<const TI*>(a.delta) + (STRIDED ? b * a.sdb + dch * a.sdd : off);
+        const TI* zr = HAS_Z ? static_cast<const TI*>(a.z) + (STRIDED ? b * a.szb + dch * a.szd : off) : nullptr;
         if (full && vec_io) {
           ru[i] = ld_quad_stream(u + t);
           rd[i] = ld_quad_stream(dl + t);
-          if constexpr (HAS_Z) rz[i] = ld_quad_stream(static_cast<const TI*>(a.z) + off + t);
+          if constexpr (HAS_Z) rz[i] = ld_quad_stream(zr + t);
         } else {
           ru[i] = ld_quad_masked(u, t, L, 1);
           rd[i] = ld_quad_masked(dl, t, L, 1);
-          if constexpr (HAS_Z) rz[i] = ld_quad_masked(static_cast<const TI*>(a.z) + off, t, L, 1);
+          if constexpr (HAS_Z) rz[i] = ld_quad_masked(zr, t, L, 1);
         }
       } else {
         ru[i] = zero_quad<TI>();
@@ -356,9 +359,9 @@ __global__ void __launch_bounds__(kThreads, 3) scan_fwd_kernel(const ScanArgs a)
   }
 }
 
-template <typename TI, typename TW, int NS, bool HAS_Z, bool WRITE_OUT>
+template <typename TI, typename TW, int NS, bool HAS_Z, bool WRITE_OUT, bool STRIDED>
 cudaError_t launch_one(const ScanArgs& a, dim3 grid, cudaStream_t stream) {
-  auto kern = scan_fwd_kernel<TI, TW, NS, HAS_Z, WRITE_OUT>;
+  auto kern = scan_fwd_kernel<TI, TW, NS, HAS_Z, WRITE_OUT, STRIDED>;
   constexpr size_t smem = sizeof(FwdSmem<NS>);
   static bool attr_set = false;  // per instantiation; setting it twice is harmless
   if (!attr_set) {
@@ -375,9 +378,14 @@ cudaError_t launch_typed(ScanArgs a, bool write_out, cudaStream_t stream) {
   constexpr int CPC = FwdShape<NS>::kCPC;
   a.tiles = (int)((a.dpg + CPC - 1) / CPC);
   const dim3 grid((unsigned)(a.tiles * a.batch * a.ngroups));
-  if (!write_out) return launch_one<TI, TW, NS, false, false>(a, grid, stream);
-  if (a.z != nullptr) return launch_one<TI, TW, NS, true, true>(a, grid, stream);
-  return launch_one<TI, TW, NS, false, true>(a, grid, stream);
+  if (io_rows_strided(a)) {
+    if (!write_out) return launch_one<TI, TW, NS, false, false, true>(a, grid, stream);
+    if (a.z != nullptr) return launch_one<TI, TW, NS, true, true, true>(a, grid, stream);
+    return launch_one<TI, TW, NS, false, true, true>(a, grid, stream);
+  }
+  if (!write_out) return launch_one<TI, TW, NS, false, false, false>(a, grid, stream);
+  if (a.z != nullptr) return launch_one<TI, TW, NS, true, true, false>(a, grid, stream);
+  return launch_one<TI, TW, NS, false, true, false>(a, grid, stream);
 }
 
 template <typename TI, typename TW>

@@ -51,6 +51,8 @@ class ScanFwdParams(ctypes.Structure):
         ("C_batch_stride", _i64), ("C_group_stride", _i64), ("C_dstate_stride", _i64),
         ("C_seqlen_stride", _i64),
         ("io_dtype", _i32), ("bc_dtype", _i32), ("delta_softplus", _i32), ("reserved", _i32),
+        ("u_batch_stride", _i64), ("u_dim_stride", _i64), ("delta_batch_stride", _i64),
+        ("delta_dim_stride", _i64), ("z_batch_stride", _i64), ("z_dim_stride", _i64),
     ]
 
 

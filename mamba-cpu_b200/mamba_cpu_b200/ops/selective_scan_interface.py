@@ -40,10 +40,26 @@ def _fwd_params(u, delta, A, B, C, D, z, delta_bias, delta_softplus):
     p.batch, p.dim, p.seqlen, p.dstate, p.ngroups = batch, dim, seqlen, dstate, ngroups
     (p.B_batch_stride, p.B_group_stride, p.B_dstate_stride, p.B_seqlen_stride) = B.stride()
     (p.C_batch_stride, p.C_group_stride, p.C_dstate_stride, p.C_seqlen_stride) = C.stride()
+    # u / delta / z may be views with their own batch and dim strides (seqlen-contiguous rows)
+    p.u_batch_stride, p.u_dim_stride = u.stride(0), u.stride(1)
+    p.delta_batch_stride, p.delta_dim_stride = delta.stride(0), delta.stride(1)
+    if z is not None:
+        p.z_batch_stride, p.z_dim_stride = z.stride(0), z.stride(1)
     p.io_dtype = _lib.dtype_code(u.dtype)
     p.bc_dtype = _lib.dtype_code(B.dtype)
     p.delta_softplus = int(bool(delta_softplus))
     return p
+
+
+def _dense(t):
+    """A contiguous tensor of t's shape and dtype (the kernels write dense rows; empty_like would
+    copy the strides of a view)."""
+    return torch.empty_like(t, memory_format=torch.contiguous_format)
+
+
+def _seqlen_rows(t):
+    """(batch, dim, seqlen) rows the kernels can read in place: unit stride along seqlen."""
+    return t.shape[-1] <= 1 or t.stride(-1) == 1
 
 
 def _check_op_inputs(name, u, delta, A, B, C, D, z, delta_bias):
@@ -52,10 +68,11 @@ def _check_op_inputs(name, u, delta, A, B, C, D, z, delta_bias):
     if u.dtype not in (torch.float32, torch.bfloat16, torch.float16):
         raise TypeError(f"{name}: u must be float32, bfloat16 or float16")
     for t, nm in ((delta, "delta"), (z, "z")):
-        if t is not None and (t.dtype != u.dtype or t.shape != u.shape or not t.is_contiguous()):
-            raise ValueError(f"{name}: {nm} must be a contiguous tensor of u's shape and dtype")
-    if not u.is_contiguous():
-        raise ValueError(f"{name}: u must be contiguous")
+        if t is not None and (t.dtype != u.dtype or t.shape != u.shape):
+            raise ValueError(f"{name}: {nm} must have u's shape and dtype")
+    for t, nm in ((u, "u"), (delta, "delta"), (z, "z")):
+        if t is not None and not _seqlen_rows(t):
+            raise ValueError(f"{name}: {nm} must be contiguous along seqlen (any batch / dim strides)")
     for t, nm in ((A, "A"), (D, "D"), (delta_bias, "delta_bias")):
         if t is not None and (t.dtype != torch.float32 or not t.is_contiguous()):
             raise ValueError(f"{name}: {nm} must be contiguous float32")
@@ -94,7 +111,7 @@ def _run_fwd(name, u, delta, A, B, C, D, z, delta_bias, delta_softplus, initial_
     batch, dim, seqlen = u.shape
     dstate = B.shape[2]
     _check_state(name, "initial_state", initial_state, batch, dim, dstate)
-    out = torch.empty_like(u)
+    out = _dense(u)
     last_state = u.new_empty(batch, dim, dstate, dtype=torch.float32)
     chunk_states = u.new_empty(batch, dim, _nchunks(seqlen), dstate, dtype=torch.float32)
     p = _fwd_params(u, delta, A, B, C, D, z, delta_bias, delta_softplus)
@@ -111,7 +128,7 @@ def _(u, delta, A, B, C, D, z, delta_bias, delta_softplus):
     batch, dim, seqlen = u.shape
     dstate = B.shape[2]
     return (
-        torch.empty_like(u),
+        _dense(u),
         u.new_empty(batch, dim, dstate, dtype=torch.float32),
         u.new_empty(batch, dim, _nchunks(seqlen), dstate, dtype=torch.float32),
     )
@@ -157,13 +174,13 @@ def _run_bwd(name, u, delta, A, B, C, D, z, delta_bias, delta_softplus, dout, dl
     if chunk_states is not None and (chunk_states.dtype != torch.float32 or not chunk_states.is_contiguous()
                                      or chunk_states.shape != (batch, dim, _nchunks(seqlen), dstate)):
         raise ValueError(f"{name}: chunk_states must come from selective_scan_fwd")
-    du = torch.empty_like(u)
-    ddelta = torch.empty_like(delta)
+    du = _dense(u)
+    ddelta = _dense(delta)
     dA = torch.empty_like(A)
     dB = torch.empty(B.shape, dtype=torch.float32, device=u.device)
     dC = torch.empty(C.shape, dtype=torch.float32, device=u.device)
     dD = u.new_empty(dim, dtype=torch.float32)
-    dz = torch.empty_like(z) if z is not None else u.new_empty(0)
+    dz = _dense(z) if z is not None else u.new_empty(0)
     ddelta_bias = u.new_empty(dim, dtype=torch.float32)
     _check_state(name, "initial_state", initial_state, batch, dim, dstate)
     dinit = u.new_empty(batch, dim, dstate, dtype=torch.float32) if initial_state is not None else u.new_empty(0)
@@ -189,10 +206,10 @@ def _run_bwd(name, u, delta, A, B, C, D, z, delta_bias, delta_softplus, dout, dl
 def _(u, delta, A, B, C, D, z, delta_bias, delta_softplus, dout, dlast_state, chunk_states):
     dim = u.shape[1]
     return (
-        torch.empty_like(u), torch.empty_like(delta), torch.empty_like(A),
+        _dense(u), _dense(delta), torch.empty_like(A),
         u.new_empty(B.shape, dtype=torch.float32), u.new_empty(C.shape, dtype=torch.float32),
         u.new_empty(dim, dtype=torch.float32),
-        torch.empty_like(z) if z is not None else u.new_empty(0),
+        _dense(z) if z is not None else u.new_empty(0),
         u.new_empty(dim, dtype=torch.float32),
     )
 
@@ -209,7 +226,7 @@ def _setup_context(ctx, inputs, output):
 
 def _backward(ctx, grad_out, grad_last_state, grad_chunk_states):
     u, delta, A, B, C, D, z, delta_bias, chunk_states = ctx.saved_tensors
-    dout = torch.zeros_like(u) if grad_out is None else grad_out.to(u.dtype).contiguous()
+    dout = _dense(u).zero_() if grad_out is None else grad_out.to(u.dtype).contiguous()
     dlast = None if grad_last_state is None else grad_last_state.float().contiguous()
     du, ddelta, dA, dB, dC, dD, dz, ddelta_bias = torch.ops.mamba_b200.selective_scan_bwd(
         u, delta, A, B, C, D, z, delta_bias, ctx.delta_softplus, dout, dlast, chunk_states
@@ -259,7 +276,7 @@ def _(u, delta, A, B, C, D, z, delta_bias, delta_softplus, initial_state):
     batch, dim, seqlen = u.shape
     dstate = B.shape[2]
     return (
-        torch.empty_like(u),
+        _dense(u),
         u.new_empty(batch, dim, dstate, dtype=torch.float32),
         u.new_empty(batch, dim, _nchunks(seqlen), dstate, dtype=torch.float32),
     )
@@ -293,10 +310,10 @@ def _selective_scan_bwd_init(
 def _(u, delta, A, B, C, D, z, delta_bias, delta_softplus, dout, dlast_state, chunk_states, initial_state):
     dim = u.shape[1]
     return (
-        torch.empty_like(u), torch.empty_like(delta), torch.empty_like(A),
+        _dense(u), _dense(delta), torch.empty_like(A),
         u.new_empty(B.shape, dtype=torch.float32), u.new_empty(C.shape, dtype=torch.float32),
         u.new_empty(dim, dtype=torch.float32),
-        torch.empty_like(z) if z is not None else u.new_empty(0),
+        _dense(z) if z is not None else u.new_empty(0),
         u.new_empty(dim, dtype=torch.float32),
         torch.empty_like(initial_state),
     )
@@ -311,7 +328,7 @@ def _setup_context_init(ctx, inputs, output):
 
 def _backward_init(ctx, grad_out, grad_last_state, grad_chunk_states):
     u, delta, A, B, C, D, z, delta_bias, chunk_states, initial_state = ctx.saved_tensors
-    dout = torch.zeros_like(u) if grad_out is None else grad_out.to(u.dtype).contiguous()
+    dout = _dense(u).zero_() if grad_out is None else grad_out.to(u.dtype).contiguous()
     dlast = None if grad_last_state is None else grad_last_state.float().contiguous()
     du, ddelta, dA, dB, dC, dD, dz, ddelta_bias, dinit = torch.ops.mamba_b200.selective_scan_bwd_init(
         u, delta, A, B, C, D, z, delta_bias, ctx.delta_softplus, dout, dlast, chunk_states, initial_state
@@ -332,6 +349,18 @@ torch.library.register_autograd(
 
 
 _IO_DTYPES = (torch.float32, torch.bfloat16, torch.float16)
+
+
+def _as_rows(X: torch.Tensor, io_dtype) -> torch.Tensor:
+    # u / delta / z: a view whose rows are seqlen-contiguous and 16-byte aligned is read in place
+    # (no copy of e.g. a transposed projection output or a chunk of in_proj's output); anything
+    # else is made contiguous.
+    X = X.to(io_dtype)
+    es = X.element_size()
+    if (_seqlen_rows(X) and X.data_ptr() % 16 == 0 and (X.stride(0) * es) % 16 == 0
+            and (X.stride(1) * es) % 16 == 0):
+        return X
+    return X.contiguous()
 
 
 def _as_kernel_bc(X: torch.Tensor, io_dtype) -> torch.Tensor:
@@ -388,9 +417,9 @@ def selective_scan_fn(
     if Bk.dtype != Ck.dtype:
         Bk, Ck = Bk.float(), Ck.float()
     out, last_state, _ = torch.ops.mamba_b200.selective_scan_fwd(
-        u.to(io).contiguous(), delta.to(io).contiguous(), A.float().contiguous(), Bk, Ck,
+        _as_rows(u, io), _as_rows(delta, io), A.float().contiguous(), Bk, Ck,
         None if D is None else D.float().contiguous(),
-        None if z is None else z.to(io).contiguous(),
+        None if z is None else _as_rows(z, io),
         None if delta_bias is None else delta_bias.float().contiguous(),
         bool(delta_softplus),
     )
