@@ -18,8 +18,10 @@
 //     lane walks its K steps backwards accumulating the gradients. The state loop is not unrolled
 //     (the body stays in the instruction cache); its per-state carries (gh entering the chunk and
 //     the lane's dA partial) live in shared memory;
-//   * dB/dC (sums over channels) are reduced deterministically: a reduce-scatter over the CW
-//     channel lanes of the warp (shuffles), a sum over the warps of the CTA (shared memory), a
+//   * dB/dC (sums over channels) are reduced deterministically: a sum over the CW channel lanes
+//     of the warp (with 8 segments: through Tensor Memory, each lane storing its values in its
+//     own TMEM lane and reading back a 16x256b fragment that holds the 4 channels of one segment;
+//     with 16 segments: a shuffle reduce-scatter), a sum over the warps of the CTA (shared memory), a
 //     sum over the CTAs of a thread-block cluster (distributed shared memory), and finally a sum
 //     over clusters by the reduce kernel below. dA / dD / ddelta_bias leave the kernel as
 //     per-row partials and are summed over batch by the same reduce kernel.
@@ -57,11 +59,13 @@ __device__ __forceinline__ void cluster_wait_acquire() {
 }
 
 // TMEM columns per CTA: per thread, the adjoint gh entering the current chunk (columns 0..15),
-// the dA partial of each state (16..31), and the chunk's u, softplus' and dz factor items
-// (32.., 3 x K columns) that the output stage reads back.
-constexpr uint32_t kTmemCols = 64;
+// the dA partial of each state (16..31), the chunk's u, softplus' and dz factor items (32.., 3 x K
+// columns) that the output stage reads back, and (64..79) the staging area of the dB / dC sum
+// over a warp's channels. At most 3 CTAs are resident per SM: 384 of the 512 columns.
+constexpr uint32_t kTmemCols = 128;
 constexpr int kColDA = kMaxState;
 constexpr int kColItems = 2 * kMaxState;
+constexpr int kColRS = 64;
 
 template <typename TW, int CPC>
 struct BwdSmem {
@@ -376,6 +380,30 @@ __device__ __forceinline__ void bwd_chunk(const BwdArgs& a, BwdSmem<TW, kBwdWarp
         v[K + i + 1] = vc.y;
       }
       dAc[j] += dA2.x + dA2.y;
+      if constexpr (S == 8) {
+        // Sum of v over the warp's 4 channel lanes (lane = channel * 8 + segment) through TMEM:
+        // each lane stores its 16 values in its own TMEM lane, then two 16x256b loads hand lane
+        // t the rows of all 4 channels of segment t / 4 at columns 2 (t % 4) + {0, 1} (dB items)
+        // and 8 + 2 (t % 4) + {0, 1} (dC items). Channels are added in order 0, 1, 2, 3.
+        tmem_st16(tcar + kColRS, v);
+        tmem_wait_st();
+        float lo[8], hi[8];
+        tmem_ld16x256b_x2(tcar + kColRS, lo);                 // channels 0, 1
+        tmem_ld16x256b_x2(tcar + kColRS + (16u << 16), hi);   // channels 2, 3
+        tmem_wait_ld();
+        const float2 sb = __fadd2_rn(__fadd2_rn(__fadd2_rn(make_float2(lo[0], lo[1]), make_float2(lo[2], lo[3])),
+                                                make_float2(hi[0], hi[1])),
+                                     make_float2(hi[2], hi[3]));
+        const float2 sc = __fadd2_rn(__fadd2_rn(__fadd2_rn(make_float2(lo[4], lo[5]), make_float2(lo[6], lo[7])),
+                                                make_float2(hi[4], hi[5])),
+                                     make_float2(hi[6], hi[7]));
+        const int pos = (lane >> 2) * K + 2 * (lane & 3);
+        if (n < N) {
+          *reinterpret_cast<float2*>(&sm.red[warp][(n * 2) * kChunk + pos]) = sb;
+          *reinterpret_cast<float2*>(&sm.red[warp][(n * 2 + 1) * kChunk + pos]) = sc;
+        }
+        continue;
+      }
       int io = 0;
 #pragma unroll
       for (int r = 0; r < R; ++r) {

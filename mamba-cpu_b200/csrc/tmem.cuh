@@ -110,4 +110,20 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) 
       : "memory");
 }
 
+// Warp-wide: 16 lanes x 16 columns starting at TMEM address taddr (whose lane field selects the
+// first of the 16 lanes) into 8 registers per thread, spread across threads (shape 16x256b, .x2).
+// Thread t receives, with r = lane (taddr) + t / 4 and c = 2 (t % 4):
+//   v[0], v[1] = (r, c), (r, c + 1)          v[2], v[3] = (r + 8, c), (r + 8, c + 1)
+//   v[4], v[5] = (r, c + 8), (r, c + 9)      v[6], v[7] = (r + 8, c + 8), (r + 8, c + 9)
+// (checked on a B200 by storing lane * 100 + column with 32x32b and reading it back this way).
+__device__ __forceinline__ void tmem_ld16x256b_x2(uint32_t taddr, float (&v)[8]) {
+  uint32_t r[8];
+  asm volatile("tcgen05.ld.sync.aligned.16x256b.x2.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr)
+               : "memory");
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 }  // namespace mb200
