@@ -19,9 +19,9 @@
 //     (the body stays in the instruction cache); its per-state carries (gh entering the chunk and
 //     the lane's dA partial) live in shared memory;
 //   * dB/dC (sums over channels) are reduced deterministically: a sum over the CW channel lanes
-//     of the warp (with 8 segments: through Tensor Memory, each lane storing its values in its
-//     own TMEM lane and reading back a 16x256b fragment that holds the 4 channels of one segment;
-//     with 16 segments: a shuffle reduce-scatter), a sum over the warps of the CTA (shared memory), a
+//     of the warp through Tensor Memory (each lane stores its values in its own TMEM lane and reads
+//     back a 16x256b fragment that holds all channel lanes of its segments), a sum over the warps
+//     of the CTA (shared memory), a
 //     sum over the CTAs of a thread-block cluster (distributed shared memory), and finally a sum
 //     over clusters by the reduce kernel below. dA / dD / ddelta_bias leave the kernel as
 //     per-row partials and are summed over batch by the same reduce kernel.
@@ -401,6 +401,26 @@ __device__ __forceinline__ void bwd_chunk(const BwdArgs& a, BwdSmem<TW, kBwdWarp
         if (n < N) {
           *reinterpret_cast<float2*>(&sm.red[warp][(n * 2) * kChunk + pos]) = sb;
           *reinterpret_cast<float2*>(&sm.red[warp][(n * 2 + 1) * kChunk + pos]) = sc;
+        }
+        continue;
+      }
+      if constexpr (S == 16) {
+        // 2 channel lanes per segment (lane = channel * 16 + segment): the same TMEM transpose
+        // with 8 columns. Lane t receives both channels of segments t / 4 and t / 4 + 8 at
+        // columns 2 (t % 4) + {0, 1}: dB items (t % 4 < 2) or dC items, 2 (t % 2) + {0, 1}.
+        tmem_st_n<2 * K>(tcar + kColRS, v);
+        tmem_wait_st();
+        float lo[4], hi[4];
+        tmem_ld16x256b_x1(tcar + kColRS, lo);                 // channel 0: segments g, g + 8
+        tmem_ld16x256b_x1(tcar + kColRS + (16u << 16), hi);   // channel 1
+        tmem_wait_ld();
+        const float2 s0 = __fadd2_rn(make_float2(lo[0], lo[1]), make_float2(hi[0], hi[1]));
+        const float2 s1 = __fadd2_rn(make_float2(lo[2], lo[3]), make_float2(hi[2], hi[3]));
+        const int g = lane >> 2, m = lane & 3;
+        const int base = (n * 2 + (m >> 1)) * kChunk + 2 * (m & 1);
+        if (n < N) {
+          *reinterpret_cast<float2*>(&sm.red[warp][base + g * K]) = s0;
+          *reinterpret_cast<float2*>(&sm.red[warp][base + (g + 8) * K]) = s1;
         }
         continue;
       }

@@ -116,6 +116,17 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) 
 //   v[0], v[1] = (r, c), (r, c + 1)          v[2], v[3] = (r + 8, c), (r + 8, c + 1)
 //   v[4], v[5] = (r, c + 8), (r, c + 9)      v[6], v[7] = (r + 8, c + 8), (r + 8, c + 9)
 // (checked on a B200 by storing lane * 100 + column with 32x32b and reading it back this way).
+// The first 8 columns only (shape 16x256b, .x1): v[0..3] as above.
+__device__ __forceinline__ void tmem_ld16x256b_x1(uint32_t taddr, float (&v)[4]) {
+  uint32_t r[4];
+  asm volatile("tcgen05.ld.sync.aligned.16x256b.x1.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(taddr)
+               : "memory");
+#pragma unroll
+  for (int i = 0; i < 4; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 __device__ __forceinline__ void tmem_ld16x256b_x2(uint32_t taddr, float (&v)[8]) {
   uint32_t r[8];
   asm volatile("tcgen05.ld.sync.aligned.16x256b.x2.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
