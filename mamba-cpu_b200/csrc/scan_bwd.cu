@@ -132,8 +132,6 @@ __device__ __forceinline__ void bwd_chunk(const BwdArgs& a, BwdSmem<TW, kBwdWarp
                                           uint32_t tcar, ChunkItems<TI, kChunk / S>& items, bool next_vec,
                                           cg::cluster_group& cluster) {
   constexpr int K = kChunk / S;
-  constexpr int CW = 32 / S;
-  constexpr int R = ilog2(CW);
   const ScanArgs& f = a.f;
   const int64_t L = f.L;
   const int N = (int)f.N;
@@ -352,7 +350,7 @@ __device__ __forceinline__ void bwd_chunk(const BwdArgs& a, BwdSmem<TW, kBwdWarp
       tmem_st2(tcar + n0, ghc[0], ghc[1]);
     }
     // -- per state: the gradient terms of the K steps (f32x2 over timestep pairs), then the
-    //    reduce-scatter of dB|dC over the CW channel lanes holding the same timesteps
+    //    sum of dB|dC over the CW channel lanes holding the same timesteps
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
       const int n = n0 + j;
@@ -402,9 +400,7 @@ __device__ __forceinline__ void bwd_chunk(const BwdArgs& a, BwdSmem<TW, kBwdWarp
           *reinterpret_cast<float2*>(&sm.red[warp][(n * 2) * kChunk + pos]) = sb;
           *reinterpret_cast<float2*>(&sm.red[warp][(n * 2 + 1) * kChunk + pos]) = sc;
         }
-        continue;
-      }
-      if constexpr (S == 16) {
+      } else {
         // 2 channel lanes per segment (lane = channel * 16 + segment): the same TMEM transpose
         // with 8 columns. Lane t receives both channels of segments t / 4 and t / 4 + 8 at
         // columns 2 (t % 4) + {0, 1}: dB items (t % 4 < 2) or dC items, 2 (t % 2) + {0, 1}.
@@ -422,26 +418,7 @@ __device__ __forceinline__ void bwd_chunk(const BwdArgs& a, BwdSmem<TW, kBwdWarp
           *reinterpret_cast<float2*>(&sm.red[warp][base + g * K]) = s0;
           *reinterpret_cast<float2*>(&sm.red[warp][base + (g + 8) * K]) = s1;
         }
-        continue;
       }
-      int io = 0;
-#pragma unroll
-      for (int r = 0; r < R; ++r) {
-        const int mask = S << r;
-        const bool upper = (lane & mask) != 0;
-        const int half = K >> r;
-#pragma unroll
-        for (int q = 0; q < half; ++q) {
-          const float send = upper ? v[q] : v[half + q];
-          const float keep = upper ? v[half + q] : v[q];
-          v[q] = keep + __shfl_xor_sync(kFull, send, mask);
-        }
-        if (r > 0 && upper) io += half;
-      }
-      const int q = (lane & S) ? 1 : 0;
-      if (n < N)
-        *reinterpret_cast<float4*>(&sm.red[warp][(n * 2 + q) * kChunk + s * K + io]) =
-            make_float4(v[0], v[1], v[2], v[3]);
     }
     tmem_st2(tcar + kColDA + n0, dAc[0], dAc[1]);
   }
@@ -572,8 +549,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3) scan_bwd_kernel(const BwdAr
   constexpr int K = kChunk / S;
   constexpr int CW = 32 / S;
   constexpr int CPC = kBwdWarps * CW;
-  static_assert(S >= 2 && S <= 16, "segments per channel");
-  static_assert((2 * K) >> ilog2(CW) == 4, "each lane ends the reduce-scatter with one float4");
+  static_assert(S == 8 || S == 16, "segments per channel: the TMEM channel sum handles 8 and 16");
   extern __shared__ __align__(128) unsigned char smem_raw[];
   BwdSmem<TW, CPC>& sm = *reinterpret_cast<BwdSmem<TW, CPC>*>(smem_raw);
 
