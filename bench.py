@@ -333,6 +333,34 @@ def run_ours(args):
         dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
     e2e_ms = float(e2e_ms.item())
 
+    # The copy floor of that e2e step on this box right now: the same step's input bytes host ->
+    # device and result bytes device -> host, both directions at once, without the compute.
+    dev_in = dbufs[0]
+    dev_out = [torch.empty_like(hb, device=dev) for hb in outs_host[0]]
+    def copies_only():
+        with torch.cuda.stream(h2d_stream):
+            for k, v in pinned.items():
+                if v is not None:
+                    dev_in[k].copy_(v, non_blocking=True)
+        with torch.cuda.stream(d2h_stream):
+            for hb, dv in zip(outs_host[0], dev_out):
+                hb.copy_(dv, non_blocking=True)
+    for _ in range(2):
+        copies_only()
+    torch.cuda.synchronize(dev)
+    c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    c0.record(comp)
+    h2d_stream.wait_event(c0)
+    d2h_stream.wait_event(c0)
+    for _ in range(e2e_steps):
+        copies_only()
+    comp.wait_stream(h2d_stream)
+    comp.wait_stream(d2h_stream)
+    c1.record(comp)
+    torch.cuda.synchronize(dev)
+    copy_floor_ms = c0.elapsed_time(c1) / e2e_steps
+    del dev_out
+
     del g_fwd, g_bwd
     torch.cuda.synchronize(dev)
     if group is not None:
@@ -386,7 +414,8 @@ def run_ours(args):
         },
         "e2e": {"value": total_E / (e2e_ms * 1e-3), "unit": "elements/s", "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": e2e_steps,
-                "timing": "CUDA events around K pipelined steps, pipeline fill and drain included"},
+                "timing": "CUDA events around K pipelined steps, pipeline fill and drain included",
+                "copy_only_ms_per_step": copy_floor_ms},
         "gpu_launches": per_step_launches * args.steps,
         "clocks": clk.summary(),
     }
