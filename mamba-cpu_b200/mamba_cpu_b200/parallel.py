@@ -5,9 +5,10 @@ csrc/selective_scan.cpp:320-324), so ranks can each own a contiguous slice of th
 u, delta, z, out, A, D, delta_bias (and their gradients) sharded along ``dim``. B and C are
 replicated: a rank passes the B / C groups its channels read (:func:`bc_groups`; all of B / C when
 ngroups = 1). The forward needs no communication. In the backward, dB and dC are sums over ALL
-channels of a group, so the partial sums of the ranks that share a group are combined with one
-all-reduce(SUM) of the fp32 [dB | dC] buffer per call, over :func:`new_reduce_group`'s process
-group. A shard holds whole groups or a part of one group, never a part of two (checked by
+channels of a group, so the partial sums of the ranks that share a group are combined once per
+call over :func:`new_reduce_group`'s process group (:func:`all_reduce_bc`: a one-kernel sum read
+from the other GPUs' memory over NVLink when the group is node-local and NCCL-backed, else one
+NCCL / gloo all_reduce). A shard holds whole groups or a part of one group, never a part of two (checked by
 :func:`shard_bounds`); a rank that holds whole groups needs no collective at all.
 
 Usage (one process per GPU, ``torch.distributed`` initialised with the NCCL backend)::
@@ -41,7 +42,7 @@ def current_group():
 @contextlib.contextmanager
 def channel_sharded(group):
     """Make selective_scan_fn calls in this context treat their channels as one shard of
-    ``group``: their backward all-reduces dB/dC across the group."""
+    ``group``: their backward sums dB/dC across the group (:func:`all_reduce_bc`)."""
     token = _group.set(group)
     try:
         yield group
