@@ -324,7 +324,7 @@ int build_conv_args(const mb200_conv1d_params* p, bool need_out, ConvArgs* a) {
   const bool empty = p->batch == 0 || p->dim == 0;
   if (!empty && (p->x == nullptr || p->weight == nullptr || (need_out && p->out == nullptr)))
     return MB200_ERR_NULL_POINTER;
-  const int64_t span = (int64_t)kConvThreads * kConvItems;
+  const int64_t span = (int64_t)kConvThreads * (kConvRowBytes / dtype_size(p->x_dtype));
   a->x = p->x;
   a->w = p->weight;
   a->bias = p->bias;

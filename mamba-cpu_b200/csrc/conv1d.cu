@@ -3,8 +3,8 @@
 // out[b, d, t] = act(bias[d] + sum_k w[d, k] * xf[b, d, t + k]), xf = [initial_states | x] (or
 // W-1 zeros in front of x), as mamba-cpu's causal_conv1d_fn computes with F.conv1d
 // (src/mamba_cpu/ops/causal_conv1d.py:37-47). The op is HBM-bound (one read of x, one write of
-// out): each thread produces 8 consecutive outputs of one row from one 16-byte-vectorised load
-// of its inputs plus a W-1 element halo served by L1.
+// out): each thread produces 32 bytes' worth of consecutive outputs of one row (8 fp32 or 16
+// 16-bit items) from two 16-byte loads of its inputs plus a W-1 element halo served by L1.
 #include "conv1d.cuh"
 
 namespace mb200 {
@@ -13,7 +13,7 @@ namespace {
 
 template <typename T, int W>
 __global__ void __launch_bounds__(kConvThreads) conv_fwd_kernel(const ConvArgs a) {
-  constexpr int J = kConvItems;
+  constexpr int J = conv_items<T>();
   constexpr int P = W - 1;
   const int64_t row = blockIdx.x / a.blocks_per_row;
   const int64_t tb = blockIdx.x % a.blocks_per_row;
@@ -69,7 +69,7 @@ __global__ void __launch_bounds__(kConvThreads) conv_fwd_kernel(const ConvArgs a
 template <typename T, int W>
 __global__ void __launch_bounds__(kConvThreads) conv_bwd_kernel(const ConvArgs a, const T* dout, T* dx,
                                                                 T* dinit, float* part) {
-  constexpr int J = kConvItems;
+  constexpr int J = conv_items<T>();
   constexpr int P = W - 1;
   __shared__ float red[kConvThreads / 32][W + 1];
   const int64_t row = blockIdx.x / a.blocks_per_row;

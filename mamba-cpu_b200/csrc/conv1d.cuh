@@ -7,7 +7,11 @@ namespace mb200 {
 
 constexpr int kConvMaxWidth = 8;
 constexpr int kConvThreads = 128;  // threads per CTA
-constexpr int kConvItems = 8;      // consecutive outputs per thread
+// Consecutive outputs per thread: 32 bytes of each input row per thread (8 fp32, 16 bf16 / fp16
+// items), so that every thread keeps two 16-byte loads per row in flight.
+constexpr int kConvRowBytes = 32;
+template <typename T>
+constexpr int conv_items() { return kConvRowBytes / (int)sizeof(T); }
 
 struct ConvArgs {
   const void* x;
