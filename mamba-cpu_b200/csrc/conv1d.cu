@@ -15,52 +15,56 @@ template <typename T, int W>
 __global__ void __launch_bounds__(kConvThreads) conv_fwd_kernel(const ConvArgs a) {
   constexpr int J = conv_items<T>();
   constexpr int P = W - 1;
-  const int64_t row = blockIdx.x / a.blocks_per_row;
+  // One CTA per (channel, span of the row); it walks the batch's rows of that channel, so a CTA
+  // streams batch x 32 bytes per thread instead of exiting after one round trip.
+  const int64_t d = blockIdx.x / a.blocks_per_row;
   const int64_t tb = blockIdx.x % a.blocks_per_row;
   const int64_t t0 = (tb * kConvThreads + threadIdx.x) * J;
   const int64_t L = a.L;
   if (t0 >= L && !(L == 0 && t0 == 0)) return;
-  const int64_t d = row % a.dim;
-  const T* xrow = static_cast<const T*>(a.x) + row * L;
-  const T* irow = a.init ? static_cast<const T*>(a.init) + row * P : nullptr;
-
-  float xv[J + P];
-#pragma unroll
-  for (int j = 0; j < P; ++j) {
-    const int64_t s = t0 - P + j;
-    xv[j] = s >= 0 ? to_f32<T>(xrow[s]) : (irow ? to_f32<T>(irow[P + s]) : 0.f);
-  }
-  {
-    float m[J];
-    load_items<T, J>(xrow, t0, L, a.vec != 0, 0.f, m);
-#pragma unroll
-    for (int i = 0; i < J; ++i) xv[P + i] = m[i];
-  }
   float w[W];
 #pragma unroll
   for (int k = 0; k < W; ++k) w[k] = a.w[d * W + k];
   const float bias = a.bias ? a.bias[d] : 0.f;
-  float o[J];
-#pragma unroll
-  for (int i = 0; i < J; ++i) {
-    float acc = bias;
-#pragma unroll
-    for (int k = 0; k < W; ++k) acc = fmaf(w[k], xv[i + k], acc);
-    o[i] = a.silu ? acc * sigmoid_f(acc) : acc;
-  }
-  store_items<T, J>(static_cast<T*>(a.out) + row * L, t0, L, a.vec != 0, o);
+  for (int64_t b = 0; b < a.batch; ++b) {
+    const int64_t row = b * a.dim + d;
+    const T* xrow = static_cast<const T*>(a.x) + row * L;
+    const T* irow = a.init ? static_cast<const T*>(a.init) + row * P : nullptr;
 
-  // The thread holding the last timestep (or thread 0 of an empty row) writes the final states:
-  // the last W-1 entries of [initial_states | x] (causal_conv1d.py:48-53).
-  if (a.final_states != nullptr && P > 0 && t0 <= (L > 0 ? L - 1 : 0) && (L == 0 || L - 1 < t0 + J)) {
-    T* frow = static_cast<T*>(a.final_states) + row * P;
+    float xv[J + P];
 #pragma unroll
     for (int j = 0; j < P; ++j) {
-      const int64_t s = L - P + j;
-      float v = s >= 0 ? to_f32<T>(xrow[s]) : (irow ? to_f32<T>(irow[P + s]) : 0.f);
-      frow[j] = from_f32<T>(v);
+      const int64_t s = t0 - P + j;
+      xv[j] = s >= 0 ? to_f32<T>(xrow[s]) : (irow ? to_f32<T>(irow[P + s]) : 0.f);
     }
-  }
+    {
+      float m[J];
+      load_items<T, J>(xrow, t0, L, a.vec != 0, 0.f, m);
+#pragma unroll
+      for (int i = 0; i < J; ++i) xv[P + i] = m[i];
+    }
+    float o[J];
+#pragma unroll
+    for (int i = 0; i < J; ++i) {
+      float acc = bias;
+#pragma unroll
+      for (int k = 0; k < W; ++k) acc = fmaf(w[k], xv[i + k], acc);
+      o[i] = a.silu ? acc * sigmoid_f(acc) : acc;
+    }
+    store_items<T, J>(static_cast<T*>(a.out) + row * L, t0, L, a.vec != 0, o);
+
+    // The thread holding the last timestep (or thread 0 of an empty row) writes the final states:
+    // the last W-1 entries of [initial_states | x] (causal_conv1d.py:48-53).
+    if (a.final_states != nullptr && P > 0 && t0 <= (L > 0 ? L - 1 : 0) && (L == 0 || L - 1 < t0 + J)) {
+      T* frow = static_cast<T*>(a.final_states) + row * P;
+#pragma unroll
+      for (int j = 0; j < P; ++j) {
+        const int64_t s = L - P + j;
+        float v = s >= 0 ? to_f32<T>(xrow[s]) : (irow ? to_f32<T>(irow[P + s]) : 0.f);
+        frow[j] = from_f32<T>(v);
+      }
+    }
+  }  // batch rows
 }
 
 // Backward: g[t] = dout[t] * act'(pre[t]);  dx[s] = sum_k w[k] g[s + P - k];
@@ -196,7 +200,7 @@ __global__ void conv_bwd_reduce(const float* part, float* dw, float* dbias, int6
 
 template <typename T, int W>
 cudaError_t fwd_w(const ConvArgs& a, cudaStream_t stream) {
-  const int64_t blocks = a.batch * a.dim * a.blocks_per_row;
+  const int64_t blocks = a.dim * a.blocks_per_row;  // each CTA walks the batch
   conv_fwd_kernel<T, W><<<(unsigned)blocks, kConvThreads, 0, stream>>>(a);
   return cudaGetLastError();
 }
