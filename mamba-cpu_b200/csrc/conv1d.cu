@@ -373,6 +373,99 @@ __global__ void __launch_bounds__(kConvThreads) conv_bwd_staged_kernel(const Con
   }
 }
 
+// Forward through the same pipeline: per stage x = [kJ items before the span | span].
+template <typename T, int W>
+__global__ void __launch_bounds__(kConvThreads) conv_fwd_staged_kernel(const ConvArgs a) {
+  using St = ConvStage<T>;
+  constexpr int J = St::kJ;
+  constexpr int P = W - 1;
+  constexpr int kXF = J + St::kSpan;  // elements per stage; kXF * sizeof(T) is a multiple of 16
+  static_assert(P <= J, "the halo holds the W - 1 items before the span");
+  extern __shared__ __align__(16) unsigned char conv_smem[];
+  T* sbuf = reinterpret_cast<T*>(conv_smem);
+  const int tid = threadIdx.x;
+  const int64_t d = blockIdx.x / a.blocks_per_row;
+  const int64_t tb = blockIdx.x % a.blocks_per_row;
+  const int64_t s0 = tb * St::kSpan;
+  const int64_t t0 = s0 + (int64_t)tid * J;
+  const int64_t L = a.L;
+  const T* x = static_cast<const T*>(a.x);
+  const T* init = static_cast<const T*>(a.init);
+  const T zero = from_f32<T>(0.f);
+  float w[W];
+#pragma unroll
+  for (int k = 0; k < W; ++k) w[k] = a.w[d * W + k];
+  const float bias = a.bias ? a.bias[d] : 0.f;
+
+  auto issue = [&](int64_t b, int st) {
+    T* xs = sbuf + (size_t)st * kXF;
+    const int64_t row = b * a.dim + d;
+    const T* xrow = x + row * L;
+    if (t0 + J <= L) {
+      cp_async16(xs + J + tid * J, xrow + t0);
+      cp_async16(xs + J + tid * J + J / 2, xrow + t0 + J / 2);
+    } else {
+#pragma unroll
+      for (int i = 0; i < J; ++i) xs[J + tid * J + i] = t0 + i < L ? xrow[t0 + i] : zero;
+    }
+    if (tid == 0) {
+      if (s0 >= J) {
+        cp_async16(xs, xrow + s0 - J);
+        cp_async16(xs + J / 2, xrow + s0 - J / 2);
+      } else {
+        const T* irow = init ? init + row * P : nullptr;
+#pragma unroll
+        for (int i = 0; i < J; ++i) {
+          const int sidx = i - J;
+          xs[i] = (irow != nullptr && sidx >= -P) ? irow[P + sidx] : zero;
+        }
+      }
+    }
+  };
+
+#pragma unroll
+  for (int sidx = 0; sidx < kConvStages - 1; ++sidx) {
+    if (sidx < a.batch) issue(sidx, sidx);
+    cp_async_commit();
+  }
+  for (int64_t b = 0; b < a.batch; ++b) {
+    const int64_t nb = b + kConvStages - 1;
+    if (nb < a.batch) issue(nb, (int)(nb % kConvStages));
+    cp_async_commit();
+    cp_async_wait<kConvStages - 1>();
+    __syncthreads();
+    const T* xs = sbuf + (size_t)(b % kConvStages) * kXF;
+    const int64_t row = b * a.dim + d;
+    if (t0 < L || (L == 0 && t0 == 0)) {
+      float xv[J + P];
+#pragma unroll
+      for (int m = 0; m < J + P; ++m) xv[m] = to_f32<T>(xs[J + tid * J - P + m]);
+      float o[J];
+#pragma unroll
+      for (int i = 0; i < J; ++i) {
+        float acc = bias;
+#pragma unroll
+        for (int k = 0; k < W; ++k) acc = fmaf(w[k], xv[i + k], acc);
+        o[i] = a.silu ? acc * sigmoid_f(acc) : acc;
+      }
+      store_items<T, J>(static_cast<T*>(a.out) + row * L, t0, L, true, o);
+      // final states: the last W-1 entries of [initial_states | x], by the thread holding the
+      // last timestep (or thread 0 of an empty row)
+      if (a.final_states != nullptr && P > 0 && t0 <= (L > 0 ? L - 1 : 0) && (L == 0 || L - 1 < t0 + J)) {
+        const T* xrow = x + row * L;
+        const T* irow = init ? init + row * P : nullptr;
+        T* frow = static_cast<T*>(a.final_states) + row * P;
+#pragma unroll
+        for (int j = 0; j < P; ++j) {
+          const int64_t sidx = L - P + j;
+          frow[j] = sidx >= 0 ? xrow[sidx] : (irow ? irow[P + sidx] : zero);
+        }
+      }
+    }
+    __syncthreads();
+  }
+}
+
 // dw[d, k] = sum over (batch group, CTA of the row) of the partials; one thread per (d, k). The
 // register-load kernel writes one partial per (batch row, span) (groups = batch), the staged one
 // one per (channel, span) already summed over the batch (groups = 1).
@@ -396,7 +489,12 @@ __global__ void conv_bwd_reduce(const float* part, float* dw, float* dbias, int6
 template <typename T, int W>
 cudaError_t fwd_w(const ConvArgs& a, cudaStream_t stream) {
   const int64_t blocks = a.dim * a.blocks_per_row;  // each CTA walks the batch
-  conv_fwd_kernel<T, W><<<(unsigned)blocks, kConvThreads, 0, stream>>>(a);
+  if (a.vec != 0 && a.batch >= kConvStagedMinBatch) {  // as the backward: aligned rows, batch >= 8
+    const size_t smem = kConvStages * (size_t)(ConvStage<T>::kJ + ConvStage<T>::kSpan) * sizeof(T);
+    conv_fwd_staged_kernel<T, W><<<(unsigned)blocks, kConvThreads, smem, stream>>>(a);
+  } else {
+    conv_fwd_kernel<T, W><<<(unsigned)blocks, kConvThreads, 0, stream>>>(a);
+  }
   return cudaGetLastError();
 }
 

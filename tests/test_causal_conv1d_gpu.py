@@ -42,21 +42,25 @@ def test_matches_oracle_fwd_bwd(width, activation, has_bias, shape):
 @pytest.mark.parametrize("with_init", [False, True])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 @pytest.mark.parametrize("shape", [(8, 32, 256), (9, 16, 2048 + 64)])
-def test_batched_backward_pipeline_matches_oracle(width, with_init, dtype, shape):
-    """Batches of 8 or more with 16-byte aligned rows take the backward that streams a channel's
-    batch rows through shared memory (several CTAs per row and a partial last span in the second
-    shape); it must agree with the float64 oracle like the register-load kernel."""
+def test_batched_pipeline_matches_oracle(width, with_init, dtype, shape):
+    """Batches of 8 or more with 16-byte aligned rows take the forward and backward that stream a
+    channel's batch rows through shared memory (several CTAs per row and a partial last span in
+    the second shape); they must agree with the float64 oracle like the register-load kernels."""
     torch.manual_seed(3)
     x = torch.randn(*shape).to(dtype)
     w, b = torch.randn(shape[1], width), torch.randn(shape[1])
     init = torch.randn(shape[0], shape[1], width - 1).to(dtype) if with_init else None
     leaves = [t.cuda().requires_grad_() if t is not None else None for t in (x, w, b, init)]
-    out = mb.causal_conv1d_fn(leaves[0], leaves[1], leaves[2], initial_states=leaves[3], activation="silu")
+    out, fin = mb.causal_conv1d_fn(leaves[0], leaves[1], leaves[2], initial_states=leaves[3], activation="silu",
+                                   return_final_states=True)
+    xf, initf = x.float(), (init.float() if init is not None else None)
+    o64, fin64 = f64.conv1d_fwd(xf, w, b, initf, "silu", return_final_states=True)
+    tol = 1e-5 if dtype == torch.float32 else 2e-2
+    assert_close(out.float(), o64, tol, tol, "out")
+    assert_close(fin.float(), fin64, 0, 0, "final_states")
     dout = torch.randn(*shape).to(dtype)
     (out * dout.cuda()).sum().backward()
-    xf = x.float()
-    g = f64.conv1d_bwd(xf, w, b, init.float() if init is not None else None, "silu", dout.float())
-    tol = 1e-5 if dtype == torch.float32 else 2e-2
+    g = f64.conv1d_bwd(xf, w, b, initf, "silu", dout.float())
     assert_close(leaves[0].grad.float(), g["dx"], tol, tol, "dx")
     for t, k in ((leaves[1], "dweight"), (leaves[2], "dbias")):
         sc = max(1.0, float(np.abs(g[k]).max()))
