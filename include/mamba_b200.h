@@ -174,7 +174,8 @@ MB200_API int mb200_selective_scan_bwd(const mb200_scan_bwd_params* p, void* wor
  * MB200_ERR_SCRATCH_LIMIT before anything is enqueued (with fwd.chunk_states given, about a
  * batch 4 x dim 1536 x seqlen 1024 problem fits; without it roughly half that).
  * The first call on each device resolves the array's device address (a runtime query) and should
- * come before any stream capture on that device. All calls on a device share the array: calls
+ * come before any stream capture on that device; a failed lookup returns MB200_ERR_CUDA and is
+ * retried by the next call (only a successful lookup is kept). All calls on a device share the array: calls
  * whose GPU work may overlap (other streams, other host threads) race and must be serialised by
  * the caller. Nothing in the array needs clearing between calls. */
 MB200_API int mb200_selective_scan_bwd_noalloc(const mb200_scan_bwd_params* p, void* stream);
@@ -302,13 +303,16 @@ MB200_API int mb200_causal_conv1d_update(const mb200_conv1d_update_params* p, vo
  * peer_bufs / peer_pads are DEVICE arrays of `world` pointers (this rank's own at index `rank`) to
  * the ranks' exchange buffers (8 * ceil((na + nb) / 4) floats each) and signal pads (world *
  * MB200_PEER_BLOCKS uint32 each, zeroed); `counters` is this rank's device array of
- * MB200_PEER_BLOCKS uint32, zeroed, that only these calls advance (call numbers: they select the
- * slot and the values the signals carry, so the call is valid inside CUDA graphs). One kernel of
- * MB200_PEER_BLOCKS CTAs per call; CTA j of a rank waits only for CTA j of the others. The wait
- * for the other ranks is bounded by timeout_us of GPU time (<= 0: 30 s); on timeout the fault
- * word of mb200_device_fault gets bit 1 and this call's sums are unspecified (a rank arriving
- * later may get unspecified sums too; the calls after it are unaffected). All ranks must make the same sequence of calls with the same sizes, and the
- * calls of one rank on one set of buffers must not overlap (issue them on one stream).
+ * MB200_PEER_BLOCKS + 1 uint32, zeroed: the first MB200_PEER_BLOCKS are call numbers that only
+ * these calls advance (they select the slot and the values the signals carry, so the call is
+ * valid inside CUDA graphs), the last is a sticky timeout flag. One kernel of MB200_PEER_BLOCKS
+ * CTAs per call; CTA j of a rank waits only for CTA j of the others. The wait for the other ranks
+ * is bounded by timeout_us of GPU time (<= 0: 30 s); a CTA whose wait runs out writes NaN into
+ * its share of a | b instead of the sum, sets bit 1 of the fault word of mb200_device_fault and
+ * sets counters[MB200_PEER_BLOCKS] to 1 (left set; the caller reads it to refuse the result and
+ * clears it). The signals stay in step, so a late rank's own call still sums correctly. All ranks
+ * must make the same sequence of calls with the same sizes, and the calls of one rank on one set
+ * of buffers must not overlap (issue them on one stream).
  */
 #define MB200_IPC_HANDLE_BYTES 64
 #define MB200_PEER_BLOCKS 148

@@ -11,7 +11,8 @@
 // The host-side name of that array is only a stand-in for it, not a device address; the device
 // address is obtained once per device with cudaGetSymbolAddress, on that device's first call.
 // That first call therefore performs a runtime query and should be made before any stream
-// capture on that device. All calls on a device share the same array and it keeps the previous
+// capture on that device; if the query fails the call returns MB200_ERR_CUDA and the next call
+// tries again. All calls on a device share the same array and it keeps the previous
 // call's contents; the backward writes every scratch byte it later reads, so nothing has to be
 // cleared between calls. Calls whose GPU work overlaps (different streams, or several host
 // threads) race on the shared scratch and must be serialised by the caller.
@@ -28,22 +29,25 @@ constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
-struct DeviceScratch {
-  std::once_flag once;
-  void* ptr = nullptr;
-  cudaError_t err = cudaSuccess;
-};
+std::mutex g_scratch_mutex;
+void* g_scratch_ptr[kMaxDevices] = {};
 
-DeviceScratch g_scratch[kMaxDevices];
-
-// Device address of the static scratch on the current device (resolved once per device).
+// Device address of the static scratch on the current device. Only a successful lookup is kept:
+// a lookup that failed (for example one attempted during stream capture) is retried by the next
+// call instead of failing every later call on that device.
 int current_scratch(void** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return MB200_ERR_CUDA;
-  DeviceScratch& slot = g_scratch[dev];
-  std::call_once(slot.once, [&slot] { slot.err = cudaGetSymbolAddress(&slot.ptr, g_noalloc_scratch); });
-  if (slot.err != cudaSuccess || slot.ptr == nullptr) return MB200_ERR_CUDA;
-  *out = slot.ptr;
+  std::lock_guard<std::mutex> lock(g_scratch_mutex);
+  if (g_scratch_ptr[dev] == nullptr) {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || ptr == nullptr) {
+      cudaGetLastError();  // the failed query must not surface as a later call's launch error
+      return MB200_ERR_CUDA;
+    }
+    g_scratch_ptr[dev] = ptr;
+  }
+  *out = g_scratch_ptr[dev];
   return MB200_OK;
 }
 

@@ -18,6 +18,11 @@
 // signalled the call in between, which it does only after its reads of the slot (the previous
 // kernel) completed, so one signal per CTA and call suffices. The counters live in device
 // memory, so the call is valid inside CUDA graphs.
+// A CTA whose wait for another rank runs out does not sum (the other rank's slot may not hold
+// this call's partials yet): it fills its elements of a | b with NaN, sets fault bit 1 and the
+// sticky word counters[MB200_PEER_BLOCKS], which the host reads to refuse the poisoned result.
+// The signals stay in step (every CTA still signals every call), so a rank that arrives late
+// completes its own call with a correct sum.
 #include <cuda_runtime.h>
 #include <string.h>
 
@@ -122,15 +127,26 @@ __device__ __forceinline__ void exchange_pass(float* a, int64_t na, float* b, in
   }
 }
 
+// Fills this CTA's quads of [a | b] with NaN (the result of a call whose wait ran out).
+__device__ __forceinline__ void poison_pass(float* a, int64_t na, float* b, int64_t nb, bool vec) {
+  const int64_t nq = (na + nb + 3) / 4;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const float q = __int_as_float(0x7fc00000);
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nq; i += stride)
+    store_quad(a, na, b, nb, vec, i, make_float4(q, q, q, q));
+}
+
 __global__ void __launch_bounds__(kPeerThreads) peer_allreduce(float* a, int64_t na, float* b, int64_t nb,
                                                                float* const* bufs, uint32_t* const* pads,
                                                                uint32_t* counters, int rank, int world,
                                                                uint64_t timeout_ns) {
   __shared__ uint32_t s_e;
+  __shared__ int s_late;
   const int j = blockIdx.x;
   if (threadIdx.x == 0) {
     s_e = counters[j] + 1u;  // only CTA j of this rank's calls touches counters[j]
     counters[j] = s_e;
+    s_late = 0;
   }
   __syncthreads();
   const uint32_t e = s_e;
@@ -148,13 +164,18 @@ __global__ void __launch_bounds__(kPeerThreads) peer_allreduce(float* a, int64_t
     for (uint64_t it = 1; (int)(ld_acquire_sys(word) - e) < 0; ++it) {
       if (((it & 255) == 0 && global_ns() - t0 > timeout_ns) || it > timeout_ns / 64) {
         atomicOr(&g_mb200_fault, kFaultPeerTimeout);
+        atomicOr(&counters[MB200_PEER_BLOCKS], 1u);  // sticky: the host refuses this result
+        s_late = 1;
         break;
       }
       __nanosleep(100);
     }
   }
   __syncthreads();
-  exchange_pass<true>(a, na, b, nb, vec, bufs, off, rank, world);
+  if (s_late)
+    poison_pass(a, na, b, nb, vec);
+  else
+    exchange_pass<true>(a, na, b, nb, vec, bufs, off, rank, world);
 }
 
 }  // namespace

@@ -363,12 +363,10 @@ template <typename TI, typename TW, int NS, bool HAS_Z, bool WRITE_OUT, bool STR
 cudaError_t launch_one(const ScanArgs& a, dim3 grid, cudaStream_t stream) {
   auto kern = scan_fwd_kernel<TI, TW, NS, HAS_Z, WRITE_OUT, STRIDED>;
   constexpr size_t smem = sizeof(FwdSmem<NS>);
-  static bool attr_set = false;  // per instantiation; setting it twice is harmless
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    attr_set = true;
-  }
+  // The attribute belongs to the current device: set it on every launch (a host-side call of a
+  // few microseconds), so a process that runs on several GPUs gets it on each of them.
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
   kern<<<grid, kThreads, smem, stream>>>(a);
   return cudaGetLastError();
 }

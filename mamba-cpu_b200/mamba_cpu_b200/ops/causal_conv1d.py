@@ -125,13 +125,15 @@ def _backward(ctx, grad_out, grad_final):
     dx, dw, db, dinit = torch.ops.mamba_b200.causal_conv1d_bwd(x, weight, bias, initial_states, ctx.silu, dout)
     if grad_final is not None and grad_final.numel():
         # final_states[j] = [initial_states | x][seqlen + j]  (causal_conv1d.py:48-53)
+        # The sums are formed in fp32 and rounded to x's dtype once (grad_final is not rounded to
+        # bf16 / fp16 before it is added).
         P, L = grad_final.shape[-1], x.shape[-1]
-        gf = grad_final.to(x.dtype)
+        gf = grad_final.float()
         nx = min(P, L)  # entries that come from x
         if nx:
-            dx[..., L - nx:] += gf[..., P - nx:]
+            dx[..., L - nx:] = (dx[..., L - nx:].float() + gf[..., P - nx:]).to(dx.dtype)
         if P > L and initial_states is not None:
-            dinit[..., L:] += gf[..., : P - L]
+            dinit[..., L:] = (dinit[..., L:].float() + gf[..., : P - L]).to(dinit.dtype)
     return dx, dw, (db if bias is not None else None), (dinit if initial_states is not None else None), None
 
 

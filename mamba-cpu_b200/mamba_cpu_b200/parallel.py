@@ -126,10 +126,13 @@ class PeerReducer:
         self._owned = owned  # this rank's allocations and its mappings of the others'
         self.dev_bufs = torch.tensor(bufs, dtype=torch.int64, device="cuda")
         self.dev_pads = torch.tensor(pads, dtype=torch.int64, device="cuda")
-        self.counters = torch.zeros(PEER_BLOCKS, dtype=torch.int32, device="cuda")
+        # PEER_BLOCKS call numbers, then the sticky timeout flag the kernel sets when a wait ran out
+        self.counters = torch.zeros(PEER_BLOCKS + 1, dtype=torch.int32, device="cuda")
         # how long a rank's kernel waits for the others before flagging fault bit 1 (a straggler
         # that checkpoints between steps must stay under it)
         self.timeout_us = int(float(os.environ.get("MAMBA_B200_PEER_TIMEOUT_S", "30")) * 1e6)
+        self._flag_host = torch.zeros(1, dtype=torch.int32, pin_memory=True)
+        self._flag_event = None
 
     @classmethod
     def create(cls, na: int, nb: int, group):
@@ -200,17 +203,45 @@ class PeerReducer:
         dist.barrier(group=group)  # every rank has mapped every buffer before anyone signals
         return reducer
 
+    def check(self):
+        """Raise :class:`PeerExchangeTimeout` if an earlier call's wait for another rank ran out
+        (that call's sums were replaced by NaN). Waits for the flag copy of the latest call issued
+        outside graph capture; calls replayed from a CUDA graph are not tracked."""
+        if self._flag_event is None:
+            return
+        self._flag_event.synchronize()
+        if int(self._flag_host[0]) != 0:
+            raise PeerExchangeTimeout(
+                "the dB/dC peer exchange timed out waiting for another rank "
+                f"(MAMBA_B200_PEER_TIMEOUT_S = {self.timeout_us / 1e6:g} s); its sums were replaced by NaN")
+
     def all_reduce_(self, a: torch.Tensor, b: torch.Tensor):
-        """Sum ``a`` and ``b`` (contiguous fp32 of the sizes given at construction) in place."""
+        """Sum ``a`` and ``b`` (contiguous fp32 of the sizes given at construction) in place.
+
+        Outside graph capture each call first checks the timeout flag left by the previous call
+        (its copy to host memory completed long before, so this does not stall the stream) and
+        raises :class:`PeerExchangeTimeout` if it is set; :meth:`check` checks the latest call."""
         from . import _lib
 
         for t, n in ((a, self.na), (b, self.nb)):
             assert t.dtype == torch.float32 and t.is_contiguous() and t.numel() == n
+        capturing = torch.cuda.is_current_stream_capturing()
+        if not capturing:
+            self.check()
         st = _lib.lib.mb200_peer_sum_f32(a.data_ptr(), self.na, b.data_ptr(), self.nb, self.dev_bufs.data_ptr(),
                                          self.dev_pads.data_ptr(), self.counters.data_ptr(), self.rank, self.world,
                                          self.timeout_us, _lib.stream_of(a))
         _lib.check(st, "mb200_peer_sum_f32")
+        if not capturing:
+            self._flag_host.copy_(self.counters[PEER_BLOCKS:], non_blocking=True)
+            if self._flag_event is None:
+                self._flag_event = torch.cuda.Event()
+            self._flag_event.record()
         return a, b
+
+
+class PeerExchangeTimeout(RuntimeError):
+    """A peer-memory dB/dC exchange gave up waiting for another rank; its result is NaN."""
 
 
 _reducers: dict = {}

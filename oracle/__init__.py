@@ -20,7 +20,9 @@ import subprocess
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_F64 = os.path.join(HERE, "_build", "liboracle.so")
 LIB_REF = os.path.join(HERE, "_ref", "libmamba_cpu_ref.so")
-REF_DIR = os.environ.get("MAMBA_REF_DIR", "/root/reference")
+# The reference checkout: $MAMBA_REF_DIR, else a directory named `reference` beside this
+# repository's checkout.
+REF_DIR = os.environ.get("MAMBA_REF_DIR", os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference"))
 
 
 def build(ref: bool = True) -> None:

@@ -27,7 +27,9 @@ import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
-REF_DIR = os.environ.get("MAMBA_REF_DIR", "/root/reference")
+# The reference checkout: $MAMBA_REF_DIR, else a directory named `reference` beside this
+# repository's checkout.
+REF_DIR = os.environ.get("MAMBA_REF_DIR", os.path.join(os.path.dirname(ROOT), "reference"))
 
 
 def _import_reference():

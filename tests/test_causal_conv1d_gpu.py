@@ -38,35 +38,64 @@ def test_matches_oracle_fwd_bwd(width, activation, has_bias, shape):
         assert_close(np64(bg.grad) / sc, g["dbias"] / sc, 1e-5, 1e-5, "dbias")
 
 
+_BATCHED = [
+    ((8, 32, 256), torch.float32), ((8, 32, 256), torch.bfloat16),
+    ((9, 16, 2048 + 64), torch.float32), ((9, 16, 2048 + 64), torch.bfloat16),
+    # rows of 16-byte but not 32-byte multiples: the thread covering the row end stages a
+    # partial span (cp.async copies mixed with plain stores)
+    ((8, 16, 2052), torch.float32), ((8, 16, 2056), torch.bfloat16),
+]
+
+
 @pytest.mark.parametrize("width", [2, 4, 8])
 @pytest.mark.parametrize("with_init", [False, True])
-@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-@pytest.mark.parametrize("shape", [(8, 32, 256), (9, 16, 2048 + 64)])
-def test_batched_pipeline_matches_oracle(width, with_init, dtype, shape):
+@pytest.mark.parametrize("shape,dtype", _BATCHED)
+@pytest.mark.parametrize("activation,has_bias", [("silu", True), (None, False)])
+def test_batched_pipeline_matches_oracle(width, with_init, shape, dtype, activation, has_bias):
     """Batches of 8 or more with 16-byte aligned rows take the forward and backward that stream a
     channel's batch rows through shared memory (several CTAs per row and a partial last span in
-    the second shape); they must agree with the float64 oracle like the register-load kernels."""
+    the larger shapes); they must agree with the float64 oracle like the register-load kernels."""
     torch.manual_seed(3)
     x = torch.randn(*shape).to(dtype)
-    w, b = torch.randn(shape[1], width), torch.randn(shape[1])
+    w = torch.randn(shape[1], width)
+    b = torch.randn(shape[1]) if has_bias else None
     init = torch.randn(shape[0], shape[1], width - 1).to(dtype) if with_init else None
     leaves = [t.cuda().requires_grad_() if t is not None else None for t in (x, w, b, init)]
-    out, fin = mb.causal_conv1d_fn(leaves[0], leaves[1], leaves[2], initial_states=leaves[3], activation="silu",
+    out, fin = mb.causal_conv1d_fn(leaves[0], leaves[1], leaves[2], initial_states=leaves[3], activation=activation,
                                    return_final_states=True)
     xf, initf = x.float(), (init.float() if init is not None else None)
-    o64, fin64 = f64.conv1d_fwd(xf, w, b, initf, "silu", return_final_states=True)
+    o64, fin64 = f64.conv1d_fwd(xf, w, b, initf, activation, return_final_states=True)
     tol = 1e-5 if dtype == torch.float32 else 2e-2
     assert_close(out.float(), o64, tol, tol, "out")
     assert_close(fin.float(), fin64, 0, 0, "final_states")
     dout = torch.randn(*shape).to(dtype)
     (out * dout.cuda()).sum().backward()
-    g = f64.conv1d_bwd(xf, w, b, initf, "silu", dout.float())
+    g = f64.conv1d_bwd(xf, w, b, initf, activation, dout.float())
     assert_close(leaves[0].grad.float(), g["dx"], tol, tol, "dx")
-    for t, k in ((leaves[1], "dweight"), (leaves[2], "dbias")):
+    grads = [(leaves[1], "dweight")] + ([(leaves[2], "dbias")] if has_bias else [])
+    for t, k in grads:
         sc = max(1.0, float(np.abs(g[k]).max()))
         assert_close(np64(t.grad) / sc, g[k] / sc, tol, tol, k)
     if with_init:
         assert_close(leaves[3].grad.float(), g["dinitial_states"], tol, tol, "dinitial_states")
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_final_states_gradient_rounds_once(dtype):
+    """With return_final_states, the gradient flowing into final_states is added to dx in fp32 and
+    rounded to x's dtype once: dx equals the float64 gradient of out and final_states together."""
+    torch.manual_seed(4)
+    x = torch.randn(2, 16, 64).to(dtype)
+    w = torch.randn(16, 4)
+    xg, wg = x.cuda().requires_grad_(), w.cuda().requires_grad_()
+    out, fin = mb.causal_conv1d_fn(xg, wg, activation="silu", return_final_states=True)
+    dout = torch.randn(2, 16, 64).to(dtype)
+    dfin = torch.randn(2, 16, 3)  # fp32 upstream gradient of the final states
+    torch.autograd.backward([out, fin], [dout.cuda(), dfin.cuda().to(fin.dtype)])
+    want = f64.conv1d_bwd(x.float(), w, None, None, "silu", dout.float())["dx"]
+    want[..., -3:] += np64(dfin.to(fin.dtype))
+    tol = 1e-5 if dtype == torch.float32 else 8e-3
+    assert_close(xg.grad.float(), want, tol, tol, "dx")
 
 
 def test_initial_and_final_states_chain():

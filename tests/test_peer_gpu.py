@@ -48,7 +48,7 @@ def _fake_exchange(na, nb):
     nq = (na + nb + 3) // 4
     bufs = [torch.zeros(2 * 4 * nq, device="cuda") for _ in range(2)]
     pads = [torch.zeros(2 * PEER_BLOCKS, dtype=torch.int32, device="cuda") for _ in range(2)]
-    counters = torch.zeros(PEER_BLOCKS, dtype=torch.int32, device="cuda")
+    counters = torch.zeros(PEER_BLOCKS + 1, dtype=torch.int32, device="cuda")  # + the timeout flag
     return bufs, pads, counters
 
 
@@ -80,25 +80,54 @@ def test_peer_sum_one_gpu_two_fake_ranks(na, nb):
     assert _lib.device_fault() == 0
     assert torch.equal(torch.cat([a, b]), want)
     assert bool((pads[1][:PEER_BLOCKS] == 1).all()), "rank 0 did not signal rank 1 from every CTA"
-    assert bool((counters == 1).all())
+    assert bool((counters[:PEER_BLOCKS] == 1).all())
+    assert int(counters[PEER_BLOCKS]) == 0, "no wait timed out, the flag must stay clear"
 
 
 def test_peer_wait_times_out_and_flags_fault():
     """Nothing sets the other rank's signal: the wait gives up after the timeout (0.1 s), records
-    fault bit 1, and the device stays usable."""
+    fault bit 1, poisons the result with NaN instead of summing a slot the other rank never
+    filled, sets the sticky flag word, and the device stays usable."""
     import time
 
     from mamba_cpu_b200 import _lib
+    from mamba_cpu_b200.parallel import PEER_BLOCKS
 
-    a, b = torch.ones(256, device="cuda"), torch.ones(256, device="cuda")
-    bufs, pads, counters = _fake_exchange(256, 256)
+    a, b = torch.ones(256, device="cuda"), torch.ones(250, device="cuda")
+    bufs, pads, counters = _fake_exchange(256, 250)
     t0 = time.perf_counter()
     _peer_sum_as_rank0(a, b, bufs, pads, counters, 100_000)
     elapsed = time.perf_counter() - t0
     assert _lib.device_fault() == 2
     assert 0.02 < elapsed < 20.0
+    assert bool(torch.isnan(a).all()) and bool(torch.isnan(b).all()), "a timed-out call must not return sums"
+    assert int(counters[PEER_BLOCKS]) == 1
     x = torch.arange(10, device="cuda", dtype=torch.float32)
     assert float(x.sum()) == 45.0  # the context is still usable
+
+
+def test_peer_reducer_refuses_a_timed_out_result():
+    """The host side of a timeout: PeerReducer reads the flag of its previous call and raises
+    PeerExchangeTimeout (one GPU; the reducer is assembled around a fake 2-rank exchange whose
+    other rank never signals)."""
+    from mamba_cpu_b200 import _lib, parallel
+
+    bufs, pads, counters = _fake_exchange(64, 64)
+    r = parallel.PeerReducer.__new__(parallel.PeerReducer)
+    r.na, r.nb, r.rank, r.world = 64, 64, 0, 2
+    r.dev_bufs = torch.tensor([t.data_ptr() for t in bufs], dtype=torch.int64, device="cuda")
+    r.dev_pads = torch.tensor([t.data_ptr() for t in pads], dtype=torch.int64, device="cuda")
+    r.counters = counters
+    r.timeout_us = 50_000
+    r._flag_host = torch.zeros(1, dtype=torch.int32, pin_memory=True)
+    r._flag_event = None
+    a, b = torch.ones(64, device="cuda"), torch.ones(64, device="cuda")
+    r.all_reduce_(a, b)  # times out on the device; the host learns of it at the next check
+    with pytest.raises(parallel.PeerExchangeTimeout):
+        r.check()
+    with pytest.raises(parallel.PeerExchangeTimeout):
+        r.all_reduce_(a, b)  # the next call refuses to run on a poisoned exchange
+    assert _lib.device_fault() == 2
 
 
 def _worker(rank, world, port, outdir):

@@ -309,3 +309,23 @@ def test_reference_abi_mirror_f32(ngroups, seqlen):
         w = want[k].reshape(got.shape)
         scale = max(1.0, float(np.abs(w).max()))
         assert_close(np64(got) / scale, w / scale, 1e-4, 1e-4, k)
+
+
+def test_two_devices_in_one_process():
+    """The kernels' launch attributes (dynamic shared memory) belong to a device: a process that
+    runs the scan on cuda:0 and then on cuda:1 must get correct results on both."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    inp = make_inputs(2, 64, 300, 16, 1, True, True, True, torch.float32)
+    o64, _ = f64.scan_fwd(*oracle_args(inp), delta_softplus=True)
+    want = f64.scan_bwd(*oracle_args(inp), True, np.ones((2, 64, 300), np.float32))
+    for dev in ("cuda:0", "cuda:1"):
+        leaves = {k: (None if v is None else v.to(dev).requires_grad_()) for k, v in inp.items()}
+        out = mb.selective_scan_fn(**leaves, delta_softplus=True)
+        out.sum().backward()
+        torch.cuda.synchronize(dev)
+        assert_close(out, o64, 1e-5, 1e-5, f"out on {dev}")
+        for k in ("u", "delta", "B"):
+            w = want[GRAD_OF[k]].reshape(inp[k].shape)
+            sc = max(1.0, float(np.abs(w).max()))
+            assert_close(np64(leaves[k].grad) / sc, w / sc, 1e-4, 1e-4, f"{k} on {dev}")

@@ -4,9 +4,11 @@ mb200_selective_scan_bwd_noalloc exists for callers that cannot allocate device 
 the library a workspace -- for example a host framework that owns all device memory and forbids
 allocations inside its execute callbacks. Instead of a workspace it uses a static device array
 inside the library. These tests call it through the C ABI on the same inputs as
-mb200_selective_scan_bwd (given a workspace allocated here) and require the same gradients on two
-calls in a row, the second running on the scratch the first one left behind; and they check that
-a request larger than the static scratch is refused before any work is enqueued.
+mb200_selective_scan_bwd (given a workspace allocated here) and require bit-identical gradients
+(both run the same deterministic kernels) on two calls in a row, the second running on the scratch
+the first one left behind, and across problems of different sizes whose scratch layouts differ;
+and they check that a request larger than the static scratch is refused before any work is
+enqueued.
 
 The file name makes pytest collect it after every other test module.
 """
@@ -62,27 +64,43 @@ def _chunk_states(x):
     return st
 
 
+SCRATCH_BYTES = 16 << 20  # MB200_NOALLOC_SCRATCH_BYTES
+
+
+def _run_both(x, states, stream, call):
+    """The workspace entry point and the no-allocation one on the same inputs; both run the same
+    deterministic kernels, so every gradient must agree bit for bit."""
+    p, want = _bwd_params(x, states)
+    nbytes = _lib.lib.mb200_selective_scan_bwd_workspace_size(p)
+    assert 0 < nbytes <= SCRATCH_BYTES, f"this case must fit the static scratch ({nbytes} bytes)"
+    ws = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    assert _lib.lib.mb200_selective_scan_bwd(p, _lib.ptr(ws), nbytes, stream) == 0
+    q, got = _bwd_params(x, states)
+    for t in got.values():
+        t.fill_(float("nan"))
+    assert _lib.lib.mb200_selective_scan_bwd_noalloc(q, stream) == 0
+    torch.cuda.synchronize()
+    for k in GRADS:
+        assert torch.equal(got[k], want[k]), f"call {call}: {k} differs from the workspace entry point"
+
+
 @pytest.mark.parametrize("dtype,with_states", [(torch.float32, True), (torch.bfloat16, False)])
 def test_noalloc_matches_workspace_entry_point_twice(dtype, with_states):
     x = _inputs(2, 96, 300, 16, 2, dtype)
     states = _chunk_states(x) if with_states else None
     stream = _lib.stream_of(x["u"])
-
-    p, want = _bwd_params(x, states)
-    nbytes = _lib.lib.mb200_selective_scan_bwd_workspace_size(p)
-    assert 0 < nbytes <= _lib.lib.mb200_selective_scan_bwd_workspace_size(p)
-    ws = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
-    assert _lib.lib.mb200_selective_scan_bwd(p, _lib.ptr(ws), nbytes, stream) == 0
-
     for call in range(2):  # the second call runs on whatever the first left in the static scratch
-        q, got = _bwd_params(x, states)
-        for t in got.values():
-            t.fill_(float("nan"))
-        assert _lib.lib.mb200_selective_scan_bwd_noalloc(q, stream) == 0
-        torch.cuda.synchronize()
-        for k in GRADS:
-            tol = 1e-5 if dtype == torch.float32 else 1e-2
-            torch.testing.assert_close(got[k], want[k], rtol=tol, atol=tol, msg=lambda m: f"call {call} {k}: {m}")
+        _run_both(x, states, stream, call)
+
+
+def test_noalloc_scratch_reuse_across_layouts():
+    """A larger problem, a smaller one with another layout of the scratch, then the larger one
+    again: each call must be correct whatever the previous call left in the shared array."""
+    big = _inputs(2, 192, 1000, 16, 2, torch.float32)
+    small = _inputs(1, 64, 130, 12, 1, torch.float32)
+    stream = _lib.stream_of(big["u"])
+    for call, x in enumerate((big, small, big)):
+        _run_both(x, None, stream, call)
 
 
 def test_noalloc_refuses_requests_beyond_its_scratch():
