@@ -44,6 +44,8 @@ CONFIGS = {
               "BASELINE config 5 (L=4096): fwd+bwd bf16 u/delta/B/C/z, fp32 A/D, b=2 d=5120 n=16"),
     "c5_16k": (2, 5120, 16384, 16, "bf16", True,
                "BASELINE config 5 (L=16384): fwd+bwd bf16 u/delta/B/C/z, fp32 A/D, b=2 d=5120 n=16"),
+    "c5_64k": (2, 5120, 65536, 16, "bf16", True,
+               "BASELINE config 5 (L=65536): fwd+bwd bf16 u/delta/B/C/z, fp32 A/D, b=2 d=5120 n=16"),
     "c4_layer": (8, 4096, 2048, 16, "bf16", True,
                  "BASELINE config 4 scan of one layer: fwd+bwd bf16, b=8 d_inner=4096 l=2048 n=16"),
 }
