@@ -1,25 +1,33 @@
 """Benchmark: selective_scan fwd+bwd elements/s and % of HBM peak on 1..8 B200s.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c5] [--impl ours|reference]
     python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 ... bench.py --gpus N
 
-One step = one forward + backward selective scan over one batch of the configuration (default
-fp32, batch 4, dim 1536, seqlen 1024, dstate 16, z, delta_bias, softplus).
-With N GPUs every rank owns a 1536-channel shard of a dim = 1536*N problem (weak scaling): the
-forward needs no communication and the backward sums the fp32 [dB | dC] partial sums over the ranks
-in one exchange: a one-kernel sum read from the other GPUs' memory over NVLink (parallel.PeerReducer;
-MAMBA_B200_PEER_REDUCE=0 selects one NCCL all_reduce instead). Inputs are resident in HBM when the timed region starts; L2 (126 MB) is flushed with a
-256 MiB write before the forward and before the backward of every step. Kernel time is taken with
-CUDA events on the launching stream (max over ranks); the step's kernels are replayed from CUDA
-graphs so host launch latency is not measured.
+One step = one forward + backward selective scan over one batch of the configuration. The default
+is BASELINE config 5 at its longest sequence (bf16 u/delta/B/C/z, fp32 A/D, batch 2, dim 5120,
+seqlen 65536, dstate 16, z, softplus), strong-scaled: with N GPUs every rank owns 5120/N channels
+of the same problem. The forward needs no communication; the backward sums the fp32 [dB | dC]
+partial sums over the ranks in one exchange (a one-kernel sum read from the other GPUs' memory over
+NVLink, parallel.PeerReducer; MAMBA_B200_PEER_REDUCE=0 selects one NCCL all_reduce). At N > 1 rank 0
+checks one step's exchanged dB / dC against the rank-ordered sum of the all-gathered partials
+("exchange_check") and the exchange alone is timed ("exchange_us_per_step").
+
+Inputs are resident in HBM when the timed region starts. Configurations whose inputs exceed L2
+(126 MB) are not flushed; smaller ones get a 256 MiB write before the forward and before the
+backward of every step. Kernel time is taken with CUDA events on the launching stream (max over
+ranks); each phase is replayed from a CUDA graph, so host launch latency is not measured. A
+"sustained" block repeats the step back to back for about 1.5 s under clock sampling.
 
 `e2e` runs the public API (selective_scan_fn + autograd) with the step's inputs copied from pinned
 host memory and every output and gradient copied back, all inside the timed region; consecutive
 steps are pipelined (copies of neighbouring steps overlap the current step's kernels).
 
+At N = 1 the line also carries a "c2" block: BASELINE config 2 (fp32, batch 4, dim 1536, seqlen
+1024, z, delta_bias), the north-star's fp32 configuration, with its own roofline and CPU baseline.
+
 `--impl reference` times the reference's own CPU kernel (mamba-cpu csrc/selective_scan.cpp built
 into oracle/_ref) with the reference's Python-side steps (B/C transpose to (b, g, l, n), zeroed
-dB/dC, per-batch partial sums) on the host's cores.
+dB/dC, per-batch partial sums) on the host's cores, on a bounded channel slice of the workload.
 """
 
 import argparse
@@ -35,24 +43,25 @@ sys.path.insert(0, os.path.join(ROOT, "mamba-cpu_b200"))
 sys.path.insert(0, ROOT)
 
 METRIC = "selective_scan fwd+bwd elements/s & % HBM peak at 1/2/4/8 B200"
+L2_BYTES = 126 * 1024 * 1024
 
 CONFIGS = {
-    # name: (batch, dim per rank, seqlen, dstate, dtype, has_z, description)
+    # name: (batch, global dim, seqlen, dstate, dtype, has_z, description); dim is split over ranks
+    "c5": (2, 5120, 65536, 16, "bf16", True,
+           "BASELINE config 5 (seqlen 65536): fwd+bwd bf16 u/delta/B/C/z, fp32 A/D, b=2 d=5120 n=16, softplus"),
+    "c5_16k": (2, 5120, 16384, 16, "bf16", True,
+               "BASELINE config 5 (seqlen 16384): fwd+bwd bf16 u/delta/B/C/z, fp32 A/D, b=2 d=5120 n=16, softplus"),
+    "c5_4k": (2, 5120, 4096, 16, "bf16", True,
+              "BASELINE config 5 (seqlen 4096): fwd+bwd bf16 u/delta/B/C/z, fp32 A/D, b=2 d=5120 n=16, softplus"),
     "c2": (4, 1536, 1024, 16, "f32", True,
            "BASELINE config 2: selective_scan_fn fwd+bwd fp32, b=4 d=1536 l=1024 n=16, z, delta_bias, softplus"),
-    "c5_4k": (2, 5120, 4096, 16, "bf16", True,
-              "BASELINE config 5 (L=4096): fwd+bwd bf16 u/delta/B/C/z, fp32 A/D, b=2 d=5120 n=16"),
-    "c5_16k": (2, 5120, 16384, 16, "bf16", True,
-               "BASELINE config 5 (L=16384): fwd+bwd bf16 u/delta/B/C/z, fp32 A/D, b=2 d=5120 n=16"),
-    "c5_64k": (2, 5120, 65536, 16, "bf16", True,
-               "BASELINE config 5 (L=65536): fwd+bwd bf16 u/delta/B/C/z, fp32 A/D, b=2 d=5120 n=16"),
     "c4_layer": (8, 4096, 2048, 16, "bf16", True,
                  "BASELINE config 4 scan of one layer: fwd+bwd bf16, b=8 d_inner=4096 l=2048 n=16"),
 }
 
 
 def algorithmic_bytes(b, d, l, n, s, s_bc, has_z, ngroups=1):
-    """Bytes a fwd+bwd pass must move at minimum (u/delta/z/out/grads + B/C + small params)."""
+    """Bytes a fwd / bwd pass must move at minimum (u/delta/z/out/grads + B/C + small params)."""
     E = b * d * l
     Z = 1 if has_z else 0
     fwd = E * s * (3 + Z) + 2 * b * ngroups * n * l * s_bc + 4 * (d * n + 2 * d)
@@ -70,7 +79,7 @@ def load_peak():
 
 
 def load_traffic(config):
-    """Per-element DRAM traffic of the dominant kernel from the committed ncu summary, if any."""
+    """Per-element DRAM traffic of the scan kernels from the committed ncu summaries, if any."""
     path = os.path.join(ROOT, "profiles", "roofline_traffic.txt")
     out = {}
     try:
@@ -80,26 +89,27 @@ def load_traffic(config):
                 if len(parts) == 3 and not line.startswith("#") and parts[0] == config:
                     out[parts[1]] = float(parts[2])
     except OSError:
-        return None
-    return out or None
+        return {}
+    return out
 
 
 class Clocks:
-    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+    """nvidia-smi sampling of SM clocks and throttle reasons during a timed region."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
          "clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index):
+    def __init__(self, index, interval_ms=50):
         self.index = index
+        self.interval_ms = interval_ms
         self.proc = None
 
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", str(self.interval_ms)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except Exception:
             self.proc = None
         time.sleep(0.3)
@@ -124,83 +134,91 @@ class Clocks:
     def summary(self):
         if not getattr(self, "samples", None):
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        sm = [float(p[1]) for p in self.samples if p[1].replace(".", "").isdigit()]
-        mx = [float(p[2]) for p in self.samples if p[2].replace(".", "").isdigit()]
+
+        def num(v):
+            try:
+                return float(v)
+            except ValueError:
+                return None
+
+        rec = [(num(p[1]), num(p[2]), num(p[3])) for p in self.samples]
+        sm = [r[0] for r in rec if r[0] is not None]
+        mx = [r[1] for r in rec if r[1] is not None]
+        pw = [r[2] for r in rec if r[2] is not None]
+        # "under load": power well above the lowest sample (taken while the GPU worked)
+        floor = min(pw) if pw else 0.0
+        loaded = [r[0] for r in rec if r[0] is not None and r[2] is not None and r[2] > floor + 100.0]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for p in self.samples for i in range(4) if p[4 + i].lower() == "active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(self.samples)}
+        return {"sm_mhz": statistics.median(loaded or sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.samples), "samples_under_load": len(loaded),
+                "interval_ms": self.interval_ms}
 
 
-def make_inputs(cfg, device, rank, torch):
-    b, d, l, n, dt_name, has_z, _ = cfg
+def make_inputs(cfg, lo, hi, device, torch, seed=1000):
+    """Seeded synthetic inputs with the BASELINE distributions for channels [lo, hi) of the
+    configuration (B / C are shared by all channels and identical on every rank)."""
+    b, _, l, n, dt_name, has_z, _ = cfg
     dt = {"f32": torch.float32, "bf16": torch.bfloat16}[dt_name]
-    g = torch.Generator().manual_seed(1000 + rank)  # per-shard channels
-    gs = torch.Generator().manual_seed(7)  # B, C are replicated across shards
-    u = torch.randn(b, d, l, generator=g).to(dt)
-    delta = torch.randn(b, d, l, generator=g).to(dt)
-    z = torch.randn(b, d, l, generator=g).to(dt) if has_z else None
-    dout = torch.randn(b, d, l, generator=g).to(dt)
-    B = torch.randn(b, 1, n, l, generator=gs).to(dt)
-    C = torch.randn(b, 1, n, l, generator=gs).to(dt)
-    D = torch.randn(d, generator=g)
-    bias = torch.rand(d, generator=g) * 3 - 4
+    d = hi - lo
+    g = torch.Generator(device=device).manual_seed(seed + lo)  # this slice's channels
+    gs = torch.Generator(device=device).manual_seed(7)          # B, C: the same on every rank
+
+    def randn(*shape, gen=g):
+        return torch.randn(*shape, generator=gen, device=device).to(dt)
+
+    u, delta = randn(b, d, l), randn(b, d, l)
+    z = randn(b, d, l) if has_z else None
+    dout = randn(b, d, l)
+    B, C = randn(b, 1, n, l, gen=gs), randn(b, 1, n, l, gen=gs)
+    D = torch.randn(d, generator=g, device=device)
     if dt_name == "f32":
-        A = -torch.arange(1, n + 1, dtype=torch.float32).repeat(d, 1)  # config 2: -exp(log(1..16))
+        bias = torch.rand(d, generator=g, device=device) * 3 - 4  # config 2: U(-4, -1)
+        A = -torch.arange(1, n + 1, dtype=torch.float32, device=device).repeat(d, 1)  # -exp(log(1..16))
     else:
-        A = -(torch.rand(d, n, generator=g) * 15.5 + 0.5)  # config 5: -U(0.5, 16)
-    host = dict(u=u, delta=delta, A=A, B=B, C=C, D=D, z=z, delta_bias=bias, dout=dout)
-    return host
+        bias = None  # config 5 has no delta_bias
+        A = -(torch.rand(d, n, generator=g, device=device) * 15.5 + 0.5)  # -U(0.5, 16)
+    return dict(u=u, delta=delta, A=A, B=B, C=C, D=D, z=z, delta_bias=bias, dout=dout)
 
 
-def run_ours(args):
-    import torch
-    import torch.distributed as dist
+def shard(cfg, rank, world):
+    """Channels [lo, hi) of this rank: the global dim split in equal contiguous shards."""
+    per = cfg[1] // world
+    if per * world != cfg[1]:
+        raise SystemExit(f"dim {cfg[1]} is not divisible by {world} ranks")
+    return rank * per, (rank + 1) * per
 
-    import mamba_cpu_b200 as mb
-    from mamba_cpu_b200 import _lib
-    from mamba_cpu_b200 import parallel
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world != args.gpus:
-        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    group = None
-    if world > 1:
-        import datetime
+def device_timing(cfg, args, ctx, sustain_s=1.5):
+    """Device-timed fwd + bwd steps of this rank's shard; returns a dict of per-step times (max over
+    ranks), launch counts, the L2 policy and the clock records of the timed and sustained regions."""
+    torch, dev, rank, world, group = ctx["torch"], ctx["dev"], ctx["rank"], ctx["world"], ctx["group"]
+    dist = ctx["dist"]
+    from mamba_cpu_b200 import _lib, parallel
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-        group = dist.group.WORLD
-
-    cfg = CONFIGS[args.config]
-    b, d, l, n, dt_name, has_z, desc = cfg
-    host = make_inputs(cfg, dev, rank, torch)
-    x = {k: (None if v is None else v.to(dev)) for k, v in host.items()}
+    b, _, l, n, dt_name, has_z, _ = cfg
+    lo, hi = shard(cfg, rank, world)
+    x = make_inputs(cfg, lo, hi, dev, torch)
     s = 4 if dt_name == "f32" else 2
-    fwd_bytes, bwd_bytes = algorithmic_bytes(b, d, l, n, s, s, has_z)
-    E = b * d * l
-    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
-
+    big = b * (hi - lo) * l * s > L2_BYTES
+    flush = None if big else torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
     ops = torch.ops.mamba_b200
     launches = {}
+    args_in = [x[k] for k in ("u", "delta", "A", "B", "C", "D", "z", "delta_bias")]
 
     def fwd():
-        r = ops.selective_scan_fwd(x["u"], x["delta"], x["A"], x["B"], x["C"], x["D"], x["z"], x["delta_bias"], True)
+        r = ops.selective_scan_fwd(*args_in, True)
         launches["fwd"] = _lib.last_launch_count()
         return r
 
-    def bwd(chunk_states):
-        r = ops.selective_scan_bwd(x["u"], x["delta"], x["A"], x["B"], x["C"], x["D"], x["z"], x["delta_bias"],
-                                   True, x["dout"], None, chunk_states)
+    def bwd(chunk_states, exchange=True):
+        r = ops.selective_scan_bwd(*args_in, True, x["dout"], None, chunk_states)
         launches["bwd"] = _lib.last_launch_count()
-        if group is not None:
+        if group is not None and exchange:
             parallel.all_reduce_bc(r[3], r[4], group)
+            launches["bwd"] += 1
         return r
 
-    # warm up, then capture one graph per phase
     stream = torch.cuda.Stream(device=dev)
     stream.wait_stream(torch.cuda.current_stream(dev))
     with torch.cuda.stream(stream):
@@ -214,14 +232,15 @@ def run_ours(args):
         fo = fwd()
     with torch.cuda.graph(g_bwd):
         bo = bwd(fo[2])
-    per_step_launches = launches["fwd"] + launches["bwd"]
 
     def step(events):
-        flush.zero_()
+        if flush is not None:
+            flush.zero_()
         events[0].record()
         g_fwd.replay()
         events[1].record()
-        flush.zero_()
+        if flush is not None:
+            flush.zero_()
         events[2].record()
         g_bwd.replay()
         events[3].record()
@@ -232,37 +251,90 @@ def run_ours(args):
     if group is not None:
         dist.barrier()
     torch.cuda.synchronize(dev)
-    with Clocks(local) as clk:
+    with Clocks(ctx["local"]) as clk:
         for i in range(args.steps):
             step(evs[i])
         torch.cuda.synchronize(dev)
     if group is not None:
         dist.barrier()
-    t_fwd = [e[0].elapsed_time(e[1]) for e in evs]
-    t_bwd = [e[2].elapsed_time(e[3]) for e in evs]
-    ms_fwd = sum(t_fwd) / len(t_fwd)
-    ms_bwd = sum(t_bwd) / len(t_bwd)
-    ms_step = ms_fwd + ms_bwd
-    stat = torch.tensor([ms_step, ms_fwd, ms_bwd], dtype=torch.float64, device=dev)
+    ms_fwd = sum(e[0].elapsed_time(e[1]) for e in evs) / len(evs)
+    ms_bwd = sum(e[2].elapsed_time(e[3]) for e in evs) / len(evs)
+
+    # sustained: the same steps back to back for about sustain_s, under clock sampling
+    n_sus = max(args.steps, int(sustain_s / max((ms_fwd + ms_bwd) * 1e-3, 1e-6)))
+    if group is not None:
+        n_t = torch.tensor([n_sus], dtype=torch.int64, device=dev)
+        dist.all_reduce(n_t, op=dist.ReduceOp.MAX)
+        n_sus = int(n_t.item())
+    # (per-phase events as in the timed region, so an L2 flush between phases is not counted)
+    sev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(n_sus)]
+    if group is not None:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    with Clocks(ctx["local"]) as clk_sus:
+        for i in range(n_sus):
+            step(sev[i])
+        torch.cuda.synchronize(dev)
+    ms_sus = sum(e[0].elapsed_time(e[1]) + e[2].elapsed_time(e[3]) for e in sev) / n_sus
+    del sev
+
+    stat = torch.tensor([ms_fwd, ms_bwd, ms_sus], dtype=torch.float64, device=dev)
     if group is not None:
         dist.all_reduce(stat, op=dist.ReduceOp.MAX)
-    ms_step, ms_fwd, ms_bwd = stat.tolist()
+    ms_fwd, ms_bwd, ms_sus = stat.tolist()
+    out = dict(ms_fwd=ms_fwd, ms_bwd=ms_bwd, ms_step=ms_fwd + ms_bwd, launches=launches["fwd"] + launches["bwd"],
+               clocks=clk.summary(), sustained={"ms_per_step": ms_sus, "steps": n_sus,
+                                                "clocks": clk_sus.summary()},
+               l2=("inputs larger than L2 (126 MB): no flush between steps" if big else
+                   "flushed (256 MiB write) before the forward and before the backward of every step"),
+               x=x, lo=lo, hi=hi)
 
-    # ---- e2e through the public API: pinned H2D, fwd + autograd bwd, D2H of everything ----
-    if args.no_e2e:
-        del g_fwd, g_bwd
-        if group is not None:
-            dist.barrier()
-            dist.destroy_process_group()
-        if rank == 0:
-            print(json.dumps({"ms_fwd": ms_fwd, "ms_bwd": ms_bwd, "ms_per_step": ms_step,
-                              "value": E * world / (ms_step * 1e-3), "note": "--no-e2e run (profiling)"}))
-        return
-    # Steps are pipelined the way an input pipeline feeds a training loop: step i + 1's inputs
-    # are copied host -> device on one stream and step i - 1's results device -> host on another
-    # while step i runs on the compute stream, with two device input buffers. Every step still
-    # moves all of its inputs and results across PCIe inside the timed region.
-    pinned = {k: (None if v is None else v.pin_memory()) for k, v in host.items()}
+    if group is not None:
+        # exchange check: one step's exchanged dB / dC against the rank-ordered sum of the partials
+        r = bwd(fo[2], exchange=False)
+        part = torch.cat([r[3].reshape(-1), r[4].reshape(-1)]).clone()
+        parallel.all_reduce_bc(r[3], r[4], group)
+        got = torch.cat([r[3].reshape(-1), r[4].reshape(-1)])
+        parts = [torch.empty_like(part) for _ in range(world)]
+        dist.all_gather(parts, part, group=group)
+        want = parts[0].clone()
+        for p_ in parts[1:]:
+            want += p_
+        ok = torch.tensor([1 if torch.equal(got, want) else 0], dtype=torch.int32, device=dev)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+        out["exchange_check"] = "ok" if int(ok.item()) == 1 else "MISMATCH"
+        # the exchange alone, event-timed (max over ranks)
+        dB, dC = r[3], r[4]
+        for _ in range(3):
+            parallel.all_reduce_bc(dB, dC, group)
+        dist.barrier()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 20
+        e0.record()
+        for _ in range(reps):
+            parallel.all_reduce_bc(dB, dC, group)
+        e1.record()
+        torch.cuda.synchronize(dev)
+        us = torch.tensor([1e3 * e0.elapsed_time(e1) / reps], dtype=torch.float64, device=dev)
+        dist.all_reduce(us, op=dist.ReduceOp.MAX)
+        out["exchange_us_per_step"] = float(us.item())
+        out["exchange_bytes"] = int(part.numel() * 4)
+        del parts, want, part, got
+    del g_fwd, g_bwd, fo, bo
+    torch.cuda.synchronize(dev)
+    return out
+
+
+def e2e_timing(cfg, args, ctx, x):
+    """The public API (selective_scan_fn + autograd backward) with every input copied from pinned
+    host memory and every output and gradient copied back inside the timed region; steps pipelined
+    as an input pipeline feeds a training loop. Returns the e2e block (max over ranks)."""
+    torch, dev, group, dist = ctx["torch"], ctx["dev"], ctx["group"], ctx["dist"]
+    import mamba_cpu_b200 as mb
+    from mamba_cpu_b200 import parallel
+
+    pinned = {k: (None if v is None else v.cpu().pin_memory()) for k, v in x.items()}
     names_in = ["u", "delta", "A", "B", "C", "D", "z", "delta_bias"]
     nbuf = 2
     comp = torch.cuda.current_stream(dev)
@@ -271,159 +343,112 @@ def run_ours(args):
               for k, v in pinned.items()} for _ in range(nbuf)]
     in_ready = [torch.cuda.Event() for _ in range(nbuf)]
     in_free = [torch.cuda.Event() for _ in range(nbuf)]
-    out_ready = [torch.cuda.Event() for _ in range(nbuf)]
+    out_ready = torch.cuda.Event()
     for ev in in_free:
         ev.record(comp)
-    outs_host = [[] for _ in range(nbuf)]
+    outs_host = []  # one set: D2H of consecutive steps are ordered on d2h_stream
 
     def issue_h2d(i):
-        b = i % nbuf
-        h2d_stream.wait_event(in_free[b])
+        bi = i % nbuf
+        h2d_stream.wait_event(in_free[bi])
         with torch.cuda.stream(h2d_stream):
             for k, v in pinned.items():
                 if v is not None:
-                    dbufs[b][k].copy_(v, non_blocking=True)
-        in_ready[b].record(h2d_stream)
+                    dbufs[bi][k].copy_(v, non_blocking=True)
+        in_ready[bi].record(h2d_stream)
 
     def compute(i):
-        b = i % nbuf
-        comp.wait_event(in_ready[b])
-        dv = dbufs[b]
+        bi = i % nbuf
+        comp.wait_event(in_ready[bi])
+        dv = dbufs[bi]
         leaves = {k: (None if dv[k] is None else dv[k].detach().requires_grad_()) for k in names_in}
         with parallel.channel_sharded(group):
             out = mb.selective_scan_fn(**leaves, delta_softplus=True)
         out.backward(dv["dout"])
         res = [out.detach()] + [leaves[k].grad for k in names_in if leaves[k] is not None]
-        in_free[b].record(comp)
-        out_ready[b].record(comp)
+        in_free[bi].record(comp)
+        out_ready.record(comp)
         return res
 
-    def issue_d2h(i, res):
-        b = i % nbuf
-        if not outs_host[b]:
-            outs_host[b] = [torch.empty(r.shape, dtype=r.dtype, pin_memory=True) for r in res]
-        d2h_stream.wait_event(out_ready[b])
+    def issue_d2h(res):
+        if not outs_host:
+            outs_host.extend(torch.empty(r.shape, dtype=r.dtype, pin_memory=True) for r in res)
+        d2h_stream.wait_event(out_ready)
         with torch.cuda.stream(d2h_stream):
-            for hbuf, r in zip(outs_host[b], res):
+            for hbuf, r in zip(outs_host, res):
                 hbuf.copy_(r, non_blocking=True)
                 r.record_stream(d2h_stream)
 
-    def run_pipeline(n):
+    def run_pipeline(nsteps):
         issue_h2d(0)
-        for i in range(n):
-            if i + 1 < n:
+        for i in range(nsteps):
+            if i + 1 < nsteps:
                 issue_h2d(i + 1)
-            issue_d2h(i, compute(i))
+            issue_d2h(compute(i))
         comp.wait_stream(d2h_stream)
 
     h2d = sum(v.numel() * v.element_size() for v in pinned.values() if v is not None)
     run_pipeline(max(args.warmup, 3))
     torch.cuda.synchronize(dev)
-    d2h = sum(v.numel() * v.element_size() for v in outs_host[0])
-    e2e_steps = max(3, args.steps)  # the same K steps as the device-timed region
+    d2h = sum(v.numel() * v.element_size() for v in outs_host)
+    steps = max(3, args.steps)  # the same K steps as the device-timed region
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if group is not None:
         dist.barrier()
     torch.cuda.synchronize(dev)
     e0.record(comp)
     h2d_stream.wait_event(e0)
-    run_pipeline(e2e_steps)
+    run_pipeline(steps)
     e1.record(comp)
     torch.cuda.synchronize(dev)
-    e2e_ms = torch.tensor([e0.elapsed_time(e1) / e2e_steps], dtype=torch.float64, device=dev)
-    if group is not None:
-        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
-    e2e_ms = float(e2e_ms.item())
+    ms = torch.tensor([e0.elapsed_time(e1) / steps], dtype=torch.float64, device=dev)
 
-    # The copy floor of that e2e step on this box right now: the same step's input bytes host ->
-    # device and result bytes device -> host, both directions at once, without the compute.
+    # the copy floor of that step on this box right now: the same bytes both ways, no compute
     dev_in = dbufs[0]
-    dev_out = [torch.empty_like(hb, device=dev) for hb in outs_host[0]]
+    dev_out = [torch.empty_like(hb, device=dev) for hb in outs_host]
+
     def copies_only():
         with torch.cuda.stream(h2d_stream):
             for k, v in pinned.items():
                 if v is not None:
                     dev_in[k].copy_(v, non_blocking=True)
         with torch.cuda.stream(d2h_stream):
-            for hb, dv in zip(outs_host[0], dev_out):
-                hb.copy_(dv, non_blocking=True)
-    for _ in range(2):
-        copies_only()
+            for hb, dvv in zip(outs_host, dev_out):
+                hb.copy_(dvv, non_blocking=True)
+
+    copies_only()
     torch.cuda.synchronize(dev)
     c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     c0.record(comp)
     h2d_stream.wait_event(c0)
     d2h_stream.wait_event(c0)
-    for _ in range(e2e_steps):
+    for _ in range(steps):
         copies_only()
     comp.wait_stream(h2d_stream)
     comp.wait_stream(d2h_stream)
     c1.record(comp)
     torch.cuda.synchronize(dev)
-    copy_floor_ms = c0.elapsed_time(c1) / e2e_steps
-    del dev_out
-
-    del g_fwd, g_bwd
-    torch.cuda.synchronize(dev)
+    floor = torch.tensor([c0.elapsed_time(c1) / steps], dtype=torch.float64, device=dev)
     if group is not None:
-        dist.barrier()
-        dist.destroy_process_group()
-    if rank != 0:
-        return
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        dist.all_reduce(floor, op=dist.ReduceOp.MAX)
+    del dbufs, dev_out, pinned, outs_host
+    torch.cuda.synchronize(dev)
+    return dict(ms=float(ms.item()), copy_floor_ms=float(floor.item()), h2d=h2d, d2h=d2h, steps=steps)
 
-    peak, peak_kind = load_peak()
-    total_E = E * world
-    value = total_E / (ms_step * 1e-3)
-    achieved_bwd = bwd_bytes / (ms_bwd * 1e-3) / 1e9
-    step_gbs = (fwd_bytes + bwd_bytes) / (ms_step * 1e-3) / 1e9
-    traffic = load_traffic(args.config)
-    line = {
-        "metric": METRIC,
-        "value": value,
-        "unit": "elements/s",
-        "n_gpus": world,
-        "steps": args.steps,
-        "warmup": args.warmup,
-        "ms_per_step": ms_step,
-        "higher_is_better": True,
-        "scaling": "weak",
-        "vs_baseline": None,
-        "dtype": dt_name,
-        "data": "synthetic (seeded; BASELINE config distributions)",
-        "config": {
-            "workload": desc + ("" if world == 1 else f"; dim sharded: {d} channels per rank, global dim {d * world}"),
-            "batch": b, "dim_per_rank": d, "seqlen": l, "dstate": n, "global_dim": d * world,
-            "l2": "flushed (256 MiB write) before the forward and before the backward of every step",
-            "parallelism": f"dim-shard{world}" if world > 1 else "single",
-            **({"dB_dC_exchange": "peer-memory one-shot sum (NVLink)"
-                if os.environ.get("MAMBA_B200_PEER_REDUCE", "1") != "0" else "NCCL all_reduce"} if world > 1 else {}),
-        },
-        "tokens_per_s": b * l / (ms_step * 1e-3),
-        "ms_fwd": ms_fwd,
-        "ms_bwd": ms_bwd,
-        "hbm_frac_step": step_gbs / peak,
-        "step_algorithmic_gbs": step_gbs,
-        "roofline": {
-            "kernel": "scan_bwd_kernel + scan_bwd_reduce_kernel (the backward op)",
-            "bound": "hbm",
-            "achieved": achieved_bwd,
-            "peak": peak,
-            "unit": "GB/s",
-            "frac": achieved_bwd / peak,
-            "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback",
-            "traffic": None if traffic is None else traffic.get("bwd_bytes_per_element", 0) * E,
-            "algorithmic_bytes_per_launch": bwd_bytes,
-        },
-        "e2e": {"value": total_E / (e2e_ms * 1e-3), "unit": "elements/s", "ms_per_step": e2e_ms,
-                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": e2e_steps,
-                "timing": "CUDA events around K pipelined steps, pipeline fill and drain included",
-                "copy_only_ms_per_step": copy_floor_ms},
-        "gpu_launches": per_step_launches * args.steps,
-        "clocks": clk.summary(),
-    }
-    if world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(cfg, args.cpu_budget)
-    print(json.dumps(line), flush=True)
+
+def roofline_block(name, kernel, nbytes, ms, peak, peak_kind, traffic_per_elem, elems):
+    achieved = nbytes / (ms * 1e-3) / 1e9
+    out = {"kernel": kernel, "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+           "frac": achieved / peak, "algorithmic_bytes_per_launch": nbytes,
+           "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback"}
+    if traffic_per_elem is not None:
+        out["traffic"] = traffic_per_elem * elems
+        out["traffic_source"] = (f"profiles/roofline_traffic.txt: ncu dram__bytes_read.sum + dram__bytes_write.sum "
+                                 f"per element of the {name} kernels, same config, scaled to this launch")
+    else:
+        out["traffic"] = None
+    return out
 
 
 def _host_cores():
@@ -433,14 +458,23 @@ def _host_cores():
         return os.cpu_count() or 1
 
 
-def reference_step_fn(cfg, torch):
-    """One fwd+bwd of the reference CPU path on the config's shapes (kernel via oracle/_ref)."""
+def sample_channels(cfg, target_elems=16 * 1024 * 1024):
+    """Channels of the bounded CPU sample: about target_elems elements, a multiple of 16."""
+    b, d, l = cfg[0], cfg[1], cfg[2]
+    ch = max(16, target_elems // (b * l) // 16 * 16)
+    return min(d, ch)
+
+
+def reference_step_fn(cfg, channels, torch):
+    """One fwd+bwd of the reference CPU path on `channels` channels of the configuration (the
+    reference's own kernel via oracle/_ref, with its Python-side steps)."""
     import oracle
     from oracle import f64, ref_c
 
-    b, d, l, n, dt_name, has_z, _ = cfg
-    host = make_inputs(cfg, None, 0, torch)
+    b, _, l, n, dt_name, has_z, _ = cfg
+    host = make_inputs(cfg, 0, channels, torch.device("cpu"), torch)
     f32 = {k: (None if v is None else v.float().contiguous()) for k, v in host.items()}
+    d = channels
     if oracle.ref_available():
         kind = "reference"
 
@@ -485,8 +519,9 @@ def cpu_baseline(cfg, budget_s):
         f64.set_num_threads(cores)
     except Exception:
         pass
-    step, kind = reference_step_fn(cfg, torch)
-    b, d, l = cfg[0], cfg[1], cfg[2]
+    ch = sample_channels(cfg)
+    step, kind = reference_step_fn(cfg, ch, torch)
+    b, l = cfg[0], cfg[2]
     t0 = time.perf_counter()
     step()  # warmup (bench_selective_scan.py:16-22 method)
     first = time.perf_counter() - t0
@@ -495,9 +530,9 @@ def cpu_baseline(cfg, budget_s):
     for _ in range(iters):
         step()
     dt = (time.perf_counter() - t0) / iters
-    return {"value": b * d * l / dt, "unit": "elements/s", "cores": cores, "kind": kind,
-            "sample": f"{iters} timed fwd+bwd passes (after 1 warm-up) of the full config "
-                      f"b={b} d={d} l={l}, {cores} threads, time.perf_counter",
+    return {"value": b * ch * l / dt, "unit": "elements/s", "cores": cores, "kind": kind,
+            "sample": f"{iters} timed fwd+bwd passes (after 1 warm-up) of b={b} x {ch} of the config's {cfg[1]} "
+                      f"channels x l={l}, {cores} threads, time.perf_counter",
             "ms_per_step": dt * 1e3}
 
 
@@ -510,8 +545,9 @@ def run_reference(args):
     cfg = CONFIGS[args.config]
     cores = _host_cores()
     torch.set_num_threads(cores)
-    step, kind = reference_step_fn(cfg, torch)
-    b, d, l = cfg[0], cfg[1], cfg[2]
+    ch = sample_channels(cfg)
+    step, kind = reference_step_fn(cfg, ch, torch)
+    b, l = cfg[0], cfg[2]
     for _ in range(args.warmup):
         step()
     times = []
@@ -520,18 +556,126 @@ def run_reference(args):
         step()
         times.append(time.perf_counter() - t0)
     ms = 1e3 * sum(times) / len(times)
-    value = b * d * l / (ms * 1e-3)
+    value = b * ch * l / (ms * 1e-3)
     line = {
         "metric": METRIC, "impl": "reference", "value": value, "unit": "elements/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "f32", "data": "synthetic (seeded; BASELINE config distributions)",
-        "config": {"workload": CONFIGS[args.config][6] + " (one shard-sized step on the host CPU)",
-                   "batch": b, "dim_per_rank": d, "seqlen": l, "dstate": cfg[3]},
+        "config": {"workload": cfg[6] + f" (each step: a {ch}-channel slice on the host CPU)",
+                   "batch": b, "dim": cfg[1], "sample_channels": ch, "seqlen": l, "dstate": cfg[3]},
         "cpu_baseline": {"value": value, "unit": "elements/s", "cores": cores, "kind": kind,
-                         "sample": f"{args.steps} fwd+bwd passes of b={b} d={d} l={l} after {args.warmup} warm-up"},
+                         "sample": f"{args.steps} fwd+bwd passes of b={b} x {ch} channels x l={l} after "
+                                   f"{args.warmup} warm-up, {cores} threads"},
         "e2e": {"value": value, "unit": "elements/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    group = None
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        group = dist.group.WORLD
+    ctx = dict(torch=torch, dist=dist, dev=dev, rank=rank, world=world, local=local, group=group)
+
+    cfg = CONFIGS[args.config]
+    b, D, l, n, dt_name, has_z, desc = cfg
+    dtm = device_timing(cfg, args, ctx)
+    e2e = None if args.no_e2e else e2e_timing(cfg, args, ctx, dtm["x"])
+    dtm.pop("x")
+    c2 = None
+    if world == 1 and args.config != "c2" and not args.no_c2:
+        c2 = device_timing(CONFIGS["c2"], args, ctx)
+        c2.pop("x")
+    if group is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+
+    peak, peak_kind = load_peak()
+    s = 4 if dt_name == "f32" else 2
+    per = D // world
+    E_rank = b * per * l
+    E = b * D * l
+    fwd_bytes, bwd_bytes = algorithmic_bytes(b, per, l, n, s, s, has_z)
+    traffic = load_traffic(args.config)
+    ms_step = dtm["ms_step"]
+    line = {
+        "metric": METRIC,
+        "value": E / (ms_step * 1e-3),
+        "unit": "elements/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms_step,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": dt_name,
+        "data": "synthetic (seeded; BASELINE config distributions)",
+        "config": {
+            "workload": desc + (f"; dim sharded over {world} ranks ({per} channels each)" if world > 1 else ""),
+            "batch": b, "dim": D, "dim_per_rank": per, "seqlen": l, "dstate": n,
+            "l2": dtm["l2"],
+            "parallelism": f"dim-shard{world}" if world > 1 else "single",
+            **({"dB_dC_exchange": "peer-memory one-shot sum (NVLink)"
+                if os.environ.get("MAMBA_B200_PEER_REDUCE", "1") != "0" else "NCCL all_reduce"} if world > 1 else {}),
+        },
+        "tokens_per_s": b * l / (ms_step * 1e-3),
+        "ms_fwd": dtm["ms_fwd"],
+        "ms_bwd": dtm["ms_bwd"],
+        "hbm_frac_step": (fwd_bytes + bwd_bytes) / (ms_step * 1e-3) / 1e9 / peak,
+        "roofline": roofline_block("backward", "scan_bwd_kernel + scan_bwd_reduce_kernel (the backward op, per rank)",
+                                   bwd_bytes, dtm["ms_bwd"], peak, peak_kind, traffic.get("bwd_bytes_per_element"),
+                                   E_rank),
+        "roofline_fwd": roofline_block("forward", "scan_fwd_kernel (per rank)", fwd_bytes, dtm["ms_fwd"], peak,
+                                       peak_kind, traffic.get("fwd_bytes_per_element"), E_rank),
+        "gpu_launches": dtm["launches"] * args.steps,
+        "clocks": dtm["clocks"],
+        "sustained": dict(dtm["sustained"], value=E / (dtm["sustained"]["ms_per_step"] * 1e-3)),
+    }
+    for k in ("exchange_check", "exchange_us_per_step", "exchange_bytes"):
+        if k in dtm:
+            line[k] = dtm[k]
+    if e2e is not None:
+        line["e2e"] = {"value": E / (e2e["ms"] * 1e-3), "unit": "elements/s", "ms_per_step": e2e["ms"],
+                       "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"], "steps": e2e["steps"],
+                       "timing": "CUDA events around K pipelined steps, pipeline fill and drain included "
+                                 "(per rank: its shard's copies; max over ranks)",
+                       "copy_only_ms_per_step": e2e["copy_floor_ms"]}
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(cfg, args.cpu_budget)
+    if c2 is not None:
+        cb, cD, cl_, cn = CONFIGS["c2"][:4]
+        cf, cbw = algorithmic_bytes(cb, cD, cl_, cn, 4, 4, True)
+        cE = cb * cD * cl_
+        ctr = load_traffic("c2")
+        line["c2"] = {
+            "workload": CONFIGS["c2"][6], "value": cE / (c2["ms_step"] * 1e-3), "unit": "elements/s",
+            "ms_per_step": c2["ms_step"], "ms_fwd": c2["ms_fwd"], "ms_bwd": c2["ms_bwd"], "l2": c2["l2"],
+            "hbm_frac_step": (cf + cbw) / (c2["ms_step"] * 1e-3) / 1e9 / peak,
+            "roofline": roofline_block("backward", "scan_bwd_kernel + scan_bwd_reduce_kernel (the backward op)", cbw,
+                                       c2["ms_bwd"], peak, peak_kind, ctr.get("bwd_bytes_per_element"), cE),
+            "roofline_fwd": roofline_block("forward", "scan_fwd_kernel", cf, c2["ms_fwd"], peak, peak_kind,
+                                           ctr.get("fwd_bytes_per_element"), cE),
+            "clocks": c2["clocks"], "sustained": c2["sustained"],
+        }
+        if not args.no_cpu_baseline:
+            line["c2"]["cpu_baseline"] = cpu_baseline(CONFIGS["c2"], args.cpu_budget)
     print(json.dumps(line), flush=True)
 
 
@@ -540,11 +684,12 @@ def main():
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=5)
-    p.add_argument("--config", default="c2", choices=sorted(CONFIGS))
+    p.add_argument("--config", default="c5", choices=sorted(CONFIGS))
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--no-e2e", action="store_true", help="kernel timing only (for profiler runs)")
-    p.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of CPU baseline work")
+    p.add_argument("--no-e2e", action="store_true", help="device timing only (for profiler runs)")
+    p.add_argument("--no-c2", action="store_true", help="skip the config-2 block of the N=1 line")
+    p.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU baseline work")
     args = p.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")

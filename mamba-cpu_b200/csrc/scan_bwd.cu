@@ -17,7 +17,7 @@
 //     a reverse shuffle scan of (a, gh) pairs carries gh across segments and chunks, then each
 //     lane walks its K steps backwards accumulating the gradients. The state loop is not unrolled
 //     (the body stays in the instruction cache); its per-state carries (gh entering the chunk and
-//     the lane's dA partial) live in shared memory;
+//     the lane's dA partial) live in Tensor Memory (TMEM);
 //   * dB/dC (sums over channels) are reduced deterministically: a sum over the CW channel lanes
 //     of the warp through Tensor Memory (each lane stores its values in its own TMEM lane and reads
 //     back a 16x256b fragment that holds all channel lanes of its segments), a sum over the warps
@@ -588,7 +588,8 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3) scan_bwd_kernel(const BwdAr
   const float bias = f.delta_bias ? f.delta_bias[d] : 0.f;
   const bool staged = f.vec_bc != 0;
 
-  // TMEM for the per-thread carries (warp 0 allocates; <= 4 co-resident CTAs x 32 columns)
+  // TMEM for the per-thread carries, the parked items and the channel-sum staging (warp 0
+  // allocates kTmemCols = 128 columns; at most 3 CTAs are co-resident, 384 of the SM's 512)
   if (warp == 0) tmem_alloc(&sm.tmem_base, kTmemCols);
   for (int i = threadIdx.x; i < CPC * N; i += blockDim.x) {
     const int ch = i / N, n = i % N;

@@ -5,7 +5,10 @@
 // every allocated column, i.e. each of its threads owns one lane ("row") of the allocation. The
 // accesses used here are the 32x32b shapes: thread i of the warp moves N consecutive columns of
 // lane 32 (w % 4) + i to or from N registers. Loads and stores are asynchronous: tcgen05.wait::ld
-// makes earlier loads' registers valid, tcgen05.wait::st completes earlier stores.
+// makes earlier loads' registers valid, tcgen05.wait::st completes earlier stores. The destination
+// registers of a load must not be read before its wait: code placed between the two must leave
+// them alone, and under register pressure the compiler may move or spill them (reading them
+// early), so waits follow loads closely.
 //
 // Kernels using this keep co-resident CTAs x columns <= 512, so an allocation never waits, and
 // free their columns (from the allocating warp) before the CTA exits.
