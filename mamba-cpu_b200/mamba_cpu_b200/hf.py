@@ -35,11 +35,12 @@ _saved: Optional[dict] = None
 
 
 def _rms_norm(x: torch.Tensor, weight: Optional[torch.Tensor], eps: float) -> torch.Tensor:
-    """x / rms(x) over the last dim, times weight (in fp32, returned in x's dtype)."""
-    xf = x.float()
+    """x / rms(x) over the last dim, times weight (in fp32 or wider, returned in x's dtype)."""
+    ct = torch.promote_types(x.dtype, torch.float32)
+    xf = x.to(ct)
     y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
     if weight is not None:
-        y = y * weight.float()
+        y = y * weight.to(ct)
     return y.to(x.dtype)
 
 
@@ -52,7 +53,12 @@ def mamba_inner_fn(xz, conv1d_weight, conv1d_bias, x_proj_weight, delta_proj_wei
     xz: (batch, 2 * d_inner, seqlen), the in_proj output; returns (batch, seqlen, d_model).
     ``checkpoint_lvl`` is accepted for signature compatibility (nothing is recomputed here beyond
     what the scan op's backward does itself). The optional RMS weights are falcon-mamba's
-    normalisations of dt, B and C.
+    normalisations, placed where mamba_ssm's ``MambaInnerFn.forward`` (mamba_ssm 2.2,
+    mamba_ssm/ops/selective_scan_interface.py) places them: B and C over d_state, and delta over
+    d_inner AFTER the dt projection (``dt_rms_weight`` has d_inner entries; transformers' FalconMamba
+    passes its ``dt_rms`` buffer of that size). transformers' sequential FalconMamba mixer instead
+    normalises the dt_rank features before ``dt_proj``, so its training fast path and its
+    sequential path are different functions.
     """
     batch, _, seqlen = xz.shape
     d_state = A.shape[-1]
@@ -61,10 +67,10 @@ def mamba_inner_fn(xz, conv1d_weight, conv1d_bias, x_proj_weight, delta_proj_wei
     x = causal_conv1d_fn(x, conv1d_weight.reshape(conv1d_weight.shape[0], -1), conv1d_bias, activation="silu")
     d_inner = x.shape[1]
     x_dbl = F.linear(x.transpose(1, 2).reshape(batch * seqlen, d_inner), x_proj_weight)  # (b l, r + 2n)
-    dt = x_dbl[:, :dt_rank]
+    delta = F.linear(x_dbl[:, :dt_rank], delta_proj_weight)  # (b l, d)
     if dt_rms_weight is not None:
-        dt = _rms_norm(dt, dt_rms_weight, b_c_dt_rms_eps)
-    delta = (delta_proj_weight @ dt.t()).reshape(d_inner, batch, seqlen).transpose(0, 1)  # (b, d, l)
+        delta = _rms_norm(delta, dt_rms_weight, b_c_dt_rms_eps)
+    delta = delta.reshape(batch, seqlen, d_inner).transpose(1, 2)  # (b, d, l)
 
     def _bc(M, start, bias, rms_w):
         if M is not None:
@@ -134,6 +140,13 @@ def patch_transformers() -> list:
                 continue
             _saved["globals"].setdefault((mod.__name__, name), getattr(mod, name, _MISSING))
             setattr(mod, name, values[name])
+        if model == "jamba":
+            # JambaMambaMixer.__init__ caches the availability in a module global that its forward
+            # reads (transformers/models/jamba/modeling_jamba.py); mixers built before patching
+            # would otherwise turn config.use_mamba_kernels off on their first CUDA forward.
+            _saved["globals"].setdefault((mod.__name__, "is_fast_path_available"),
+                                         getattr(mod, "is_fast_path_available", _MISSING))
+            mod.is_fast_path_available = True
         patched.append(mod.__name__)
     return patched
 

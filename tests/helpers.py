@@ -71,3 +71,37 @@ def assert_close(got, want, rtol, atol, name="", max_frac=0.0, norm_tol=None):
     if norm_tol is not None and err.size:
         scale = max(1.0, float(np.abs(w).max()))
         assert worst / scale <= norm_tol, f"{name}: max err {worst:.3e} / scale {scale:.3e} > {norm_tol}"
+
+
+def inner_fn_ref(xz, conv1d_weight, conv1d_bias, x_proj_weight, delta_proj_weight, out_proj_weight,
+                 out_proj_bias, A, B=None, C=None, D=None, delta_bias=None, B_proj_bias=None,
+                 C_proj_bias=None, delta_softplus=True, checkpoint_lvl=1, b_rms_weight=None,
+                 c_rms_weight=None, dt_rms_weight=None, b_c_dt_rms_eps=1e-6):
+    """mamba_ssm's inner function (mamba_ssm 2.2, ops/selective_scan_interface.py MambaInnerFn /
+    mamba_inner_ref) in plain PyTorch: conv1d + SiLU, x_proj, dt_proj, the RMS norms of B, C (over
+    d_state) and delta (over d_inner, after dt_proj), the selective scan, out_proj."""
+    import torch.nn.functional as F
+
+    from mamba_cpu_b200 import causal_conv1d_ref, selective_scan_ref
+
+    def rms(t, w):
+        ct = torch.promote_types(t.dtype, torch.float32)
+        tf = t.to(ct)
+        y = tf * torch.rsqrt(tf.pow(2).mean(-1, keepdim=True) + b_c_dt_rms_eps)
+        return (y if w is None else y * w.to(ct)).to(t.dtype)
+
+    r, n = delta_proj_weight.shape[1], A.shape[-1]
+    x, z = xz.chunk(2, dim=1)
+    x = causal_conv1d_ref(x, conv1d_weight.reshape(conv1d_weight.shape[0], -1), conv1d_bias, "silu")
+    x_dbl = F.linear(x.transpose(1, 2), x_proj_weight)  # (b, l, r + 2n)
+    delta = F.linear(x_dbl[..., :r], delta_proj_weight)  # (b, l, d)
+    if dt_rms_weight is not None:
+        delta = rms(delta, dt_rms_weight)
+    if B is None:
+        B = x_dbl[..., r:r + n] + (0 if B_proj_bias is None else B_proj_bias)
+        B = (B if b_rms_weight is None else rms(B, b_rms_weight)).transpose(1, 2)
+    if C is None:
+        C = x_dbl[..., r + n:r + 2 * n] + (0 if C_proj_bias is None else C_proj_bias)
+        C = (C if c_rms_weight is None else rms(C, c_rms_weight)).transpose(1, 2)
+    y = selective_scan_ref(x, delta.transpose(1, 2), A, B, C, D, z, delta_bias, delta_softplus)
+    return F.linear(y.transpose(1, 2), out_proj_weight, out_proj_bias)

@@ -73,6 +73,30 @@ def test_patch_registers_modules_and_globals():
     assert dict(hub_kernels._KERNEL_MODULE_MAPPING) == before
 
 
+@pytest.mark.parametrize("family", ["falcon_mamba", "jamba"])
+def test_patch_covers_other_families(family):
+    """FalconMamba resolves through "falcon_mamba-ssm" and falcon_mamba_inner_fn; Jamba through
+    "mamba-ssm" plus its cached is_fast_path_available flag. Both are undone by unpatching."""
+    import importlib
+
+    mod = importlib.import_module(f"transformers.models.{family}.modeling_{family}")
+    names = ["causal_conv1d_fn", "causal_conv1d_update", "selective_state_update", "selective_scan_fn",
+             "falcon_mamba_inner_fn" if family == "falcon_mamba" else "mamba_inner_fn"]
+    if family == "jamba":
+        names.append("is_fast_path_available")
+    before = {n: getattr(mod, n, "<missing>") for n in names}
+    with _patched():
+        for n in names:
+            want = True if n == "is_fast_path_available" else getattr(hf, n.replace("falcon_", ""))
+            assert getattr(mod, n) is want, n
+        if family == "falcon_mamba":
+            from transformers import FalconMambaConfig, FalconMambaModel
+
+            FalconMambaModel(FalconMambaConfig(vocab_size=32, hidden_size=16, state_size=4, num_hidden_layers=1))
+            assert mod.falcon_mamba_inner_fn is hf.mamba_inner_fn
+    assert {n: getattr(mod, n, "<missing>") for n in names} == before
+
+
 def test_mamba_inner_fn_signature_matches_mamba_ssm():
     import inspect
 
@@ -81,6 +105,39 @@ def test_mamba_inner_fn_signature_matches_mamba_ssm():
                            "out_proj_weight", "out_proj_bias", "A", "B", "C", "D"]
     for kw in ("delta_bias", "delta_softplus", "b_rms_weight", "c_rms_weight", "dt_rms_weight", "b_c_dt_rms_eps"):
         assert kw in params
+
+
+@pytest.mark.parametrize("falcon", [False, True])
+def test_mamba_inner_fn_composition(falcon, monkeypatch):
+    """The composition around the ops (conv, projections, where the RMS norms sit, B/C projection
+    biases) on CPU: hf.mamba_inner_fn with its two ops swapped for the plain-PyTorch references
+    equals mamba_ssm's inner function restated in PyTorch, outputs and gradients."""
+    from helpers import inner_fn_ref
+    from mamba_cpu_b200 import causal_conv1d_ref, selective_scan_ref
+
+    monkeypatch.setattr(hf, "causal_conv1d_fn", causal_conv1d_ref)
+    monkeypatch.setattr(hf, "selective_scan_fn", selective_scan_ref)
+    g = torch.Generator().manual_seed(5)
+    b, d, r, n, L = 2, 12, 3, 4, 9
+
+    def p(*shape, scale=0.5):
+        return (torch.randn(*shape, generator=g, dtype=torch.float64) * scale).requires_grad_()
+
+    args = [p(b, 2 * d, L), p(d, 1, 4), p(d), p(r + 2 * n, d), p(d, r), p(5, d), p(5),
+            -torch.rand(d, n, generator=g, dtype=torch.float64).add(0.5).requires_grad_()]
+    kw = dict(D=p(d), delta_bias=p(d, scale=0.1), delta_softplus=True)
+    if falcon:
+        kw.update(b_rms_weight=p(n), c_rms_weight=p(n), dt_rms_weight=p(d), b_c_dt_rms_eps=1e-6)
+    else:
+        kw.update(B_proj_bias=p(n), C_proj_bias=p(n))
+    leaves = args + [v for v in kw.values() if isinstance(v, torch.Tensor)]
+    outs = []
+    for fn in (hf.mamba_inner_fn, inner_fn_ref):
+        out = fn(*args, **kw)
+        outs.append((out.detach(), torch.autograd.grad((out * out.detach().cos()).sum(), leaves)))
+    torch.testing.assert_close(outs[0][0], outs[1][0], rtol=1e-12, atol=1e-12)
+    for ga, gb in zip(outs[0][1], outs[1][1]):
+        torch.testing.assert_close(ga, gb, rtol=1e-10, atol=1e-12)
 
 
 def _model():
