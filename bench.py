@@ -23,7 +23,10 @@ host memory and every output and gradient copied back, all inside the timed regi
 steps are pipelined (copies of neighbouring steps overlap the current step's kernels).
 
 At N = 1 the line also carries a "c2" block: BASELINE config 2 (fp32, batch 4, dim 1536, seqlen
-1024, z, delta_bias), the north-star's fp32 configuration, with its own roofline and CPU baseline.
+1024, z, delta_bias), the north-star's fp32 configuration, with its own roofline and CPU baseline;
+and "c3" / "c4" blocks: BASELINE configs 3 and 4 at model level (transformers' MambaForCausalLM,
+random init, routed to this package by hf.patch_transformers): the 130M prefill in fp32 and the
+1.4B-shape training step in bf16, in tokens/s, device-timed and end to end.
 
 `--impl reference` times the reference's own CPU kernel (mamba-cpu csrc/selective_scan.cpp built
 into oracle/_ref) with the reference's Python-side steps (B/C transpose to (b, g, l, n), zeroed
@@ -437,6 +440,104 @@ def e2e_timing(cfg, args, ctx, x):
     return dict(ms=float(ms.item()), copy_floor_ms=float(floor.item()), h2d=h2d, d2h=d2h, steps=steps)
 
 
+MODEL_CONFIGS = {
+    # BASELINE configs 3 and 4 at model level: transformers' MambaForCausalLM, random init, with
+    # hf.patch_transformers() routing its mixers to this package (the reference's hf route,
+    # mamba-cpu src/mamba_cpu/hf.py; timed end to end by its benchmarks/check_hf_model.py:25-60).
+    "c3": dict(desc="BASELINE config 3: random-init Mamba-1 130M (24 layers, d_model 768, d_inner 1536, n 16, "
+                    "dt_rank 48, vocab 50280, tied embeddings, weights N(0, 0.02)) prefill fp32, batch 1, seqlen "
+                    "1024, MambaForCausalLM through hf.patch_transformers",
+               hidden=768, layers=24, dt_rank=48, batch=1, seqlen=1024, dtype="f32", train=False),
+    "c4": dict(desc="BASELINE config 4 on one GPU: random-init Mamba-1 1.4B shape (48 layers, d_model 2048, d_inner "
+                    "4096, n 16, dt_rank 128, vocab 50280) training step (forward, loss, backward; no optimizer "
+                    "update, as the reference's check_hf_model train step) bf16, batch 8, seqlen 2048, "
+                    "MambaForCausalLM through hf.patch_transformers",
+               hidden=2048, layers=48, dt_rank=128, batch=8, seqlen=2048, dtype="bf16", train=True),
+}
+
+
+def model_timing(name, args, ctx, steps=5, warmup=3):
+    """One BASELINE model-level configuration on this GPU: device time per step (token ids
+    resident) and an end-to-end time per step through the public call with the ids copied from
+    pinned host memory and the step's result (prefill: all logits; training: the loss) copied back."""
+    torch, dev = ctx["torch"], ctx["dev"]
+    from transformers import MambaConfig, MambaForCausalLM
+
+    from mamba_cpu_b200 import hf
+
+    m = MODEL_CONFIGS[name]
+    dtype = torch.float32 if m["dtype"] == "f32" else torch.bfloat16
+    vocab = 50280
+    mcfg = MambaConfig(vocab_size=vocab, hidden_size=m["hidden"], state_size=16, num_hidden_layers=m["layers"],
+                       expand=2, conv_kernel=4, time_step_rank=m["dt_rank"], use_mambapy=False,
+                       tie_word_embeddings=True, initializer_range=0.02)
+    torch.manual_seed(0)
+    hf.patch_transformers()
+    try:
+        with torch.device(dev):
+            model = MambaForCausalLM(mcfg).to(dtype)
+        params = sum(p.numel() for p in model.parameters())
+        b, l = m["batch"], m["seqlen"]
+        g = torch.Generator().manual_seed(1)
+        ids_host = torch.randint(0, vocab, (b, l), generator=g).pin_memory()
+        ids = ids_host.to(dev)
+        model.train(m["train"])
+
+        def step(x):
+            if m["train"]:
+                model.zero_grad(set_to_none=True)
+                loss = model(x, labels=x).loss
+                loss.backward()
+                return loss.detach()
+            with torch.no_grad():
+                return model(x).logits
+
+        out_host = None
+
+        def e2e_step():
+            nonlocal out_host
+            x = ids_host.to(dev, non_blocking=True)
+            r = step(x)
+            if out_host is None:
+                out_host = torch.empty(r.shape, dtype=r.dtype, pin_memory=True)
+            out_host.copy_(r, non_blocking=True)
+            return r
+
+        for _ in range(warmup):
+            r = step(ids)
+        torch.cuda.synchronize()
+        finite = bool(torch.isfinite(r.float()).all())
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        ev[0].record()
+        for _ in range(steps):
+            step(ids)
+        ev[1].record()
+        torch.cuda.synchronize()
+        e2e_step()
+        torch.cuda.synchronize()
+        ev[2].record()
+        for _ in range(steps):
+            e2e_step()
+        ev[3].record()
+        torch.cuda.synchronize()
+        ms = ev[0].elapsed_time(ev[1]) / steps
+        ms_e2e = ev[2].elapsed_time(ev[3]) / steps
+        d2h = out_host.numel() * out_host.element_size()
+    finally:
+        hf.unpatch_transformers()
+    block = {
+        "workload": m["desc"], "value": b * l / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms,
+        "steps": steps, "warmup": warmup, "dtype": m["dtype"], "params": params,
+        "data": "synthetic (random-init weights, uniform token ids)",
+        "result_finite": finite,
+        "e2e": {"value": b * l / (ms_e2e * 1e-3), "unit": "tokens/s", "ms_per_step": ms_e2e,
+                "h2d_bytes_per_step": ids_host.numel() * ids_host.element_size(), "d2h_bytes_per_step": d2h},
+    }
+    del model
+    torch.cuda.empty_cache()
+    return block
+
+
 def roofline_block(name, kernel, nbytes, ms, peak, peak_kind, traffic_per_elem, elems):
     achieved = nbytes / (ms * 1e-3) / 1e9
     out = {"kernel": kernel, "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
@@ -445,7 +546,8 @@ def roofline_block(name, kernel, nbytes, ms, peak, peak_kind, traffic_per_elem, 
     if traffic_per_elem is not None:
         out["traffic"] = traffic_per_elem * elems
         out["traffic_source"] = (f"profiles/roofline_traffic.txt: ncu dram__bytes_read.sum + dram__bytes_write.sum "
-                                 f"per element of the {name} kernels, same config, scaled to this launch")
+                                 f"per element of the {name} kernels (config 5 captured at seqlen 4096), scaled to "
+                                 f"the elements of this launch")
     else:
         out["traffic"] = None
     return out
@@ -600,6 +702,10 @@ def run_ours(args):
     if world == 1 and args.config != "c2" and not args.no_c2:
         c2 = device_timing(CONFIGS["c2"], args, ctx)
         c2.pop("x")
+    models = {}
+    if world == 1 and not args.no_models:
+        for name in ("c3", "c4"):
+            models[name] = model_timing(name, args, ctx)
     if group is not None:
         dist.barrier()
         dist.destroy_process_group()
@@ -676,6 +782,7 @@ def run_ours(args):
         }
         if not args.no_cpu_baseline:
             line["c2"]["cpu_baseline"] = cpu_baseline(CONFIGS["c2"], args.cpu_budget)
+    line.update(models)
     print(json.dumps(line), flush=True)
 
 
@@ -689,6 +796,8 @@ def main():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true", help="device timing only (for profiler runs)")
     p.add_argument("--no-c2", action="store_true", help="skip the config-2 block of the N=1 line")
+    p.add_argument("--no-models", action="store_true",
+                   help="skip the model-level config-3 / config-4 blocks of the N=1 line")
     p.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU baseline work")
     args = p.parse_args()
     if args.warmup < 3:

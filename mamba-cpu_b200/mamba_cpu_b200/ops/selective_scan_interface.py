@@ -79,8 +79,6 @@ def _check_op_inputs(name, u, delta, A, B, C, D, z, delta_bias):
     for t, nm in ((B, "B"), (C, "C")):
         if t.dtype not in (torch.float32, u.dtype):
             raise TypeError(f"{name}: {nm} must be float32 or u's dtype")
-        if t.shape[-1] > 1 and t.stride(-1) != 1:
-            raise ValueError(f"{name}: {nm} must be contiguous along seqlen")
     if B.dtype != C.dtype:
         raise TypeError(f"{name}: B and C must share a dtype")
 
@@ -364,12 +362,16 @@ def _as_rows(X: torch.Tensor, io_dtype) -> torch.Tensor:
 
 
 def _as_kernel_bc(X: torch.Tensor, io_dtype) -> torch.Tensor:
-    # (b, n, l) or (b, g, n, l) -> (b, g, n, l) view; seqlen must be the unit-stride dim
+    # (b, n, l) or (b, g, n, l) -> (b, g, n, l) view. Seqlen-contiguous B / C are staged by the
+    # bulk-copy engine; other layouts (x_proj's slices in mamba_inner_fn have seqlen stride
+    # dt_rank + 2 * dstate) are read by per-lane loads in the kernels. For float32 that is faster
+    # than a copy (HF layout at config-2 size, fwd + bwd through autograd: 0.649 ms in place vs
+    # 0.725 ms copied); for 2-byte types the copy is faster (0.561 vs 0.663 ms), so those are copied.
     if X.dim() == 3:
         X = X.unsqueeze(1)
     if X.dtype not in (torch.float32, io_dtype):
         X = X.float()
-    if X.shape[-1] > 1 and X.stride(-1) != 1:
+    if X.shape[-1] > 1 and X.stride(-1) != 1 and X.dtype != torch.float32:
         X = X.contiguous()
     return X
 

@@ -185,3 +185,29 @@ def test_cached_generation_matches_sequential_path(family):
     with torch.no_grad(), _slow(model, family):
         ref = model.generate(ids, **kw)
     assert torch.equal(fast, ref)
+
+
+def test_config3_prefill_matches_sequential_path():
+    """BASELINE config 3 at full size: the random-init 130M MambaForCausalLM (24 layers, d_model
+    768, d_inner 1536, dt_rank 48, vocab 50280, weights N(0, 0.02)), fp32 prefill of 1024 tokens,
+    through the patched route against transformers' sequential mixer on the same GPU."""
+    torch.manual_seed(0)
+    cfg = transformers.MambaConfig(vocab_size=50280, hidden_size=768, state_size=16, num_hidden_layers=24, expand=2,
+                                   conv_kernel=4, time_step_rank=48, use_mambapy=False, tie_word_embeddings=True,
+                                   initializer_range=0.02)
+    hf.patch_transformers()
+    try:
+        with torch.device("cuda"):
+            model = transformers.MambaForCausalLM(cfg).float().eval()
+    finally:
+        hf.unpatch_transformers()
+    ids = torch.randint(0, 50280, (1, 1024), generator=torch.Generator().manual_seed(1)).cuda()
+    with torch.no_grad(), _fast(model, "mamba"):
+        fast = model(ids).logits
+    with torch.no_grad(), _slow(model, "mamba"):
+        ref = model(ids).logits
+    # fp32 through 24 layers: elementwise within 1e-3 relative, and the largest error small
+    # against the largest logit
+    assert_close(fast, ref, 1e-3, 1e-4, "logits", norm_tol=1e-4)
+    del model
+    torch.cuda.empty_cache()

@@ -113,3 +113,44 @@ def test_negative_strides_are_a_layout_error():
     p.delta_dim_stride = -seqlen
     st = _lib.lib.mb200_selective_scan_fwd(ctypes.byref(p), _lib.stream_of(u))
     assert st == 4  # MB200_ERR_BAD_LAYOUT
+
+
+def _xproj_bc(batch, seqlen, n, r, dtype, device):
+    """B / C as mamba_inner_fn slices them out of x_proj's output (b*l, r + 2n): (b, n, l) views
+    with seqlen stride r + 2n and dstate stride 1."""
+    g = torch.Generator().manual_seed(seqlen + r)
+    x_dbl = torch.randn(batch * seqlen, r + 2 * n, generator=g).to(dtype).to(device)
+    B = x_dbl[:, r:r + n].reshape(batch, seqlen, n).transpose(1, 2)
+    C = x_dbl[:, r + n:].reshape(batch, seqlen, n).transpose(1, 2)
+    return B, C
+
+
+def test_xproj_bc_slices_kept_in_place_for_float32():
+    """float32 B / C slices go to the kernels' strided path as they are; 2-byte ones are copied
+    (their per-lane strided loads are slower than a copy)."""
+    B, _ = _xproj_bc(2, 64, 16, 48, torch.float32, "cpu")
+    Bk = ssi._as_kernel_bc(B, torch.float32)
+    assert Bk.data_ptr() == B.data_ptr() and Bk.stride(-1) == 80 and Bk.shape == (2, 1, 16, 64)
+    Bh, _ = _xproj_bc(2, 64, 16, 48, torch.bfloat16, "cpu")
+    assert ssi._as_kernel_bc(Bh, torch.bfloat16).stride(-1) == 1
+    u = torch.randn(2, 8, 64)
+    ssi._check_op_inputs("t", u, u, -torch.rand(8, 16), Bk, Bk, None, None, None)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("seqlen", [256, 300])
+def test_xproj_bc_slices_match_contiguous(dtype, seqlen):
+    batch, dim, n = 2, 64, 16
+    u, delta, z = _views(batch, dim, seqlen, dtype, "cuda")
+    B, C = _xproj_bc(batch, seqlen, n, 48, dtype, "cuda")
+    g = torch.Generator().manual_seed(9)
+    A = (-torch.rand(dim, n, generator=g) * 4.0 - 0.1).cuda()
+    D = torch.randn(dim, generator=g).cuda()
+    bias = (torch.rand(dim, generator=g) * 0.5).cuda()
+    dout = torch.randn(batch, dim, seqlen, generator=g).to(dtype).cuda()
+    got = _run(u, delta, z, A, B, C, D, bias, dout)
+    want = _run(u, delta, z, A, B.contiguous(), C.contiguous(), D, bias, dout)
+    names = ("out", "du", "ddelta", "dA", "dB", "dC", "dD", "dz", "ddelta_bias")
+    for nm, a, b in zip(names, got, want):
+        torch.testing.assert_close(a, b, rtol=1e-6, atol=1e-6, msg=nm)
