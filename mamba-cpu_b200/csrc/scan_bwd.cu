@@ -825,9 +825,11 @@ cudaError_t read_fault_bwd(int* out) { return read_fault_word(out); }
 
 int bwd_cluster_size(int64_t tiles, int64_t slices) {
   // Larger clusters divide the dB/dC partials written per slice (fewer cluster partials for the
-  // reduce kernel) but constrain where CTAs may be placed. When the grid fits one wave of
-  // resident CTAs (3 per SM), 8 is best; when it takes several waves, clusters of 8 leave SMs
-  // idle at the wave boundaries and pairs are faster (measured: BASELINE config 2 vs config 5).
+  // reduce kernel) but constrain where CTAs may be placed, which costs more the more waves of
+  // resident CTAs (3 per SM) the grid takes. Measured, backward ms with 1 / 2 / 4 / 8 CTAs per
+  // cluster: config 2 (0.86 waves) 0.289 / 0.262 / 0.247 / 0.243; config 5 at L 16384 (1.44
+  // waves) 7.42 / 7.27 / 7.12 / 7.65 (L 65536: 28.88 with 2, 28.40 with 4); the config-4 layer
+  // shape (4.6 waves) 2.396 with 2, 2.434 with 4. Hence 8 up to one wave, 4 up to two, else 2.
   static int sms = 0;
   if (sms == 0) {
     int dev = 0, n = 0;
@@ -838,7 +840,7 @@ int bwd_cluster_size(int64_t tiles, int64_t slices) {
       sms = 148;
   }
   const int64_t ctas = tiles * slices;
-  const int cap = ctas <= (int64_t)sms * 3 ? kMaxCluster : 2;
+  const int cap = ctas <= (int64_t)sms * 3 ? kMaxCluster : ctas <= (int64_t)sms * 6 ? 4 : 2;
   int cl = 1;
   while (cl * 2 <= cap && tiles >= cl * 2) cl *= 2;
   return cl;
