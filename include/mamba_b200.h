@@ -150,6 +150,31 @@ typedef struct mb200_scan_bwd_params {
  * (src/mamba_cpu/ops/selective_scan_interface.py:16-40). */
 MB200_API int mb200_selective_scan_fwd(const mb200_scan_fwd_params* p, void* stream);
 
+/* Sequence pieces. When a call's whole rows give too few CTAs to fill the GPU (a small batch x dim,
+ * e.g. one rank's shard of a dim-sharded problem), the scans cut every row into pieces of whole
+ * 64-step chunks run by separate CTAs: a summary pass runs the recurrence of each piece from a
+ * zero state (forward: pieces but the last; backward: the adjoint of pieces but the first), and
+ * every piece then starts from its predecessors' composed state (the recurrence is affine in its
+ * initial state). Results agree with whole rows to rounding. The forward keeps the summaries in a
+ * workspace: mb200_selective_scan_fwd allocates it stream-ordered (cudaMallocAsync) when needed;
+ * mb200_selective_scan_fwd_ws takes it from the caller. The backward's are part of its workspace.
+ * No reference counterpart (the reference parallelises over rows only, csrc/selective_scan.cpp:
+ * 320-324). */
+/* Bytes of forward workspace for these parameters: 0 when rows are not split (or on bad
+ * arguments). */
+MB200_API size_t mb200_selective_scan_fwd_workspace_size(const mb200_scan_fwd_params* p);
+/* mb200_selective_scan_fwd with a caller workspace (256-byte aligned, at least
+ * mb200_selective_scan_fwd_workspace_size(p) bytes, need not be initialised). */
+MB200_API int mb200_selective_scan_fwd_ws(const mb200_scan_fwd_params* p, void* workspace,
+                                          size_t workspace_bytes, void* stream);
+/* Force the pieces per row of later calls (0 restores the automatic choice). Process-wide; meant
+ * for tests and tuning. */
+MB200_API void mb200_set_sequence_pieces(int pieces);
+/* The automatic choice for a grid of `ctas` CTAs over whole rows of `nchunks` chunks (or the forced
+ * count): 1 when the CTAs fill at least three quarters of the resident slots (3 per SM), else
+ * min(8, slots / ctas, nchunks / 4). */
+MB200_API int mb200_sequence_pieces(int64_t ctas, int nchunks);
+
 /* Bytes of device workspace mb200_selective_scan_bwd needs for these parameters (0 on bad
  * arguments). Depends on shapes and on whether fwd.chunk_states is NULL, not on pointer values. */
 MB200_API size_t mb200_selective_scan_bwd_workspace_size(const mb200_scan_bwd_params* p);

@@ -64,6 +64,11 @@ int build_scan_args(const mb200_scan_fwd_params* p, bool need_out, ScanArgs* a) 
   a->sCl = p->C_seqlen_stride;
   a->tiles = 0;
   a->nchunks = (int)((p->seqlen + kChunk - 1) / kChunk);
+  a->pieces = 1;
+  a->piece_chunks = a->nchunks;
+  a->piece_e = nullptr;
+  a->piece_scratch = nullptr;
+  a->piece_P = nullptr;
   a->softplus = p->delta_softplus != 0;
   const int64_t dense_b = p->dim * p->seqlen, dense_d = p->seqlen;
   auto pick = [](int64_t s, int64_t dense) { return s != 0 ? s : dense; };
@@ -89,34 +94,97 @@ int build_scan_args(const mb200_scan_fwd_params* p, bool need_out, ScanArgs* a) 
   return MB200_OK;
 }
 
+// Sequence pieces for a grid whose whole rows give `ctas` CTAs: (pieces, chunks per piece), with
+// no empty piece.
+void piece_split(int64_t ctas, int nchunks, int* pieces, int* piece_chunks) {
+  int G = nchunks > 1 ? seq_pieces(ctas, nchunks) : 1;
+  int pc = G > 1 ? (nchunks + G - 1) / G : nchunks;
+  if (G > 1) G = (nchunks + pc - 1) / pc;
+  *pieces = G;
+  *piece_chunks = pc;
+}
+
+struct FwdLayout {
+  size_t e, P, scratch, total;
+  int pieces, piece_chunks;
+};
+
+FwdLayout fwd_layout(const ScanArgs& a) {
+  FwdLayout w = {};
+  w.pieces = 1;
+  w.piece_chunks = a.nchunks;
+  if (a.batch > 0 && a.dim > 0) piece_split(fwd_ctas(a), a.nchunks, &w.pieces, &w.piece_chunks);
+  const size_t per = sizeof(float) * (size_t)(w.pieces - 1) * a.batch * a.dim * a.N;
+  ScanArgs t = a;
+  t.pieces = w.pieces;
+  t.piece_chunks = w.piece_chunks;
+  size_t off = 0;
+  w.e = off;
+  off = align_up(off + per, 256);
+  w.P = off;
+  off = align_up(off + per, 256);
+  w.scratch = off;
+  off = align_up(off + sizeof(float) * summary_scratch_floats(t), 256);
+  w.total = w.pieces > 1 ? off : 0;
+  return w;
+}
+
 struct BwdLayout {
-  size_t states, part_bc, part_A, part_D, part_db, total;
-  int cluster;
+  size_t states, part_bc, part_A, part_D, part_db, piece_G, piece_P, scratch, total;
+  int cluster, pieces, piece_chunks;
   int64_t clusters, Lpad;
 };
 
 BwdLayout bwd_layout(const ScanArgs& f, bool need_states, bool batch_partials) {
   BwdLayout w = {};
-  const int S = bwd_segments(f.batch * f.dim);
+  const int S = bwd_segments(f.batch * f.dim, f.nchunks);
   const int64_t cpc = kBwdWarps * (32 / S);
   const int64_t tiles = (f.dpg + cpc - 1) / cpc;
-  w.cluster = bwd_cluster_size(tiles, f.batch * f.ngroups);
+  const int64_t slices = f.batch * f.ngroups;
+  // batch_partials writes the caller's per-batch partial buffers directly: whole rows only
+  w.pieces = 1;
+  w.piece_chunks = f.nchunks;
+  if (!batch_partials && f.batch > 0 && f.dim > 0) piece_split(tiles * slices, f.nchunks, &w.pieces, &w.piece_chunks);
+  w.cluster = bwd_cluster_size(tiles, slices * w.pieces);
   w.clusters = (tiles + w.cluster - 1) / w.cluster;
   w.Lpad = (int64_t)f.nchunks * kChunk;
   const int64_t rows = f.batch * f.dim;
+  const int64_t G = w.pieces;
   size_t off = 0;
   w.states = off;
   if (need_states) off = align_up(off + sizeof(float) * rows * f.nchunks * f.N, 256);
   w.part_bc = off;
-  off = align_up(off + sizeof(float) * f.batch * f.ngroups * w.clusters * 2 * f.N * w.Lpad, 256);
+  off = align_up(off + sizeof(float) * slices * w.clusters * 2 * f.N * w.Lpad, 256);
   w.part_A = off;
-  if (!batch_partials) off = align_up(off + sizeof(float) * rows * f.N, 256);
+  if (!batch_partials) off = align_up(off + sizeof(float) * G * rows * f.N, 256);
   w.part_D = off;
-  if (!batch_partials) off = align_up(off + sizeof(float) * rows, 256);
+  if (!batch_partials) off = align_up(off + sizeof(float) * G * rows, 256);
   w.part_db = off;
-  if (!batch_partials) off = align_up(off + sizeof(float) * rows, 256);
+  if (!batch_partials) off = align_up(off + sizeof(float) * G * rows, 256);
+  w.piece_G = off;
+  if (G > 1) off = align_up(off + sizeof(float) * G * rows * f.N, 256);
+  w.piece_P = off;
+  if (G > 1) off = align_up(off + sizeof(float) * G * rows * f.N, 256);
+  ScanArgs t = f;
+  t.pieces = w.pieces;
+  t.piece_chunks = w.piece_chunks;
+  w.scratch = off;
+  if (G > 1) off = align_up(off + sizeof(float) * summary_scratch_floats(t), 256);
   w.total = off;
   return w;
+}
+
+int run_fwd(const mb200_scan_fwd_params* p, ScanArgs a, const FwdLayout& w, char* ws, cudaStream_t stream) {
+  a.pieces = w.pieces;
+  a.piece_chunks = w.piece_chunks;
+  if (w.pieces > 1) {
+    a.piece_e = reinterpret_cast<float*>(ws + w.e);
+    a.piece_P = reinterpret_cast<float*>(ws + w.P);
+    a.piece_scratch = reinterpret_cast<float*>(ws + w.scratch);
+  }
+  if (launch_scan_fwd(a, p->io_dtype, p->bc_dtype, true, stream) != cudaSuccess) return MB200_ERR_CUDA;
+  if (a.batch > 0 && a.dim > 0) note_launches(w.pieces > 1 ? 2 : 1);
+  return MB200_OK;
 }
 
 int check_bwd(const mb200_scan_bwd_params* p, ScanArgs* f) {
@@ -151,6 +219,13 @@ int run_bwd(const mb200_scan_bwd_params* p, ScanArgs f, char* ws, const BwdLayou
   a.part_db = batch_partials ? pdb : reinterpret_cast<float*>(ws + w.part_db);
   a.Lpad = w.Lpad;
   a.clusters = (int)w.clusters;
+  a.f.pieces = w.pieces;
+  a.f.piece_chunks = w.piece_chunks;
+  if (w.pieces > 1) {
+    a.piece_G = reinterpret_cast<float*>(ws + w.piece_G);
+    a.piece_P = reinterpret_cast<float*>(ws + w.piece_P);
+    a.f.piece_scratch = reinterpret_cast<float*>(ws + w.scratch);
+  }
   int launches = 0;
   if (p->fwd.chunk_states != nullptr) {
     a.states = p->fwd.chunk_states;
@@ -171,6 +246,10 @@ int run_bwd(const mb200_scan_bwd_params* p, ScanArgs f, char* ws, const BwdLayou
   a.f.last_state = nullptr;
   a.f.chunk_states = nullptr;
   if (f.batch > 0 && f.dim > 0) {
+    if (w.pieces > 1) {
+      if (launch_bwd_piece_summary(a, p->fwd.io_dtype, p->fwd.bc_dtype, stream) != cudaSuccess) return MB200_ERR_CUDA;
+      ++launches;
+    }
     if (launch_scan_bwd(a, p->fwd.io_dtype, p->fwd.bc_dtype, w.cluster, stream) != cudaSuccess)
       return MB200_ERR_CUDA;
     ++launches;
@@ -191,16 +270,43 @@ using namespace mb200;
 
 extern "C" {
 
+MB200_API size_t mb200_selective_scan_fwd_workspace_size(const mb200_scan_fwd_params* p) {
+  ScanArgs a;
+  if (build_scan_args(p, true, &a) != MB200_OK) return 0;
+  return fwd_layout(a).total;
+}
+
+MB200_API int mb200_selective_scan_fwd_ws(const mb200_scan_fwd_params* p, void* workspace, size_t workspace_bytes,
+                                          void* stream) {
+  reset_launches();
+  ScanArgs a;
+  int st = build_scan_args(p, true, &a);
+  if (st != MB200_OK) return st;
+  const FwdLayout w = fwd_layout(a);
+  if (w.total > 0 && (workspace == nullptr || workspace_bytes < w.total ||
+                      (reinterpret_cast<uintptr_t>(workspace) & 255) != 0))
+    return MB200_ERR_WORKSPACE;
+  return run_fwd(p, a, w, static_cast<char*>(workspace), static_cast<cudaStream_t>(stream));
+}
+
 MB200_API int mb200_selective_scan_fwd(const mb200_scan_fwd_params* p, void* stream) {
   reset_launches();
   ScanArgs a;
   int st = build_scan_args(p, true, &a);
   if (st != MB200_OK) return st;
-  if (launch_scan_fwd(a, p->io_dtype, p->bc_dtype, true, static_cast<cudaStream_t>(stream)) != cudaSuccess)
-    return MB200_ERR_CUDA;
-  if (a.batch > 0 && a.dim > 0) note_launches(1);
-  return MB200_OK;
+  // the sequence-piece summaries (small grids only) live in a stream-ordered allocation
+  const FwdLayout w = fwd_layout(a);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  void* ws = nullptr;
+  if (w.total > 0 && cudaMallocAsync(&ws, w.total, s) != cudaSuccess) return MB200_ERR_CUDA;
+  st = run_fwd(p, a, w, static_cast<char*>(ws), s);
+  if (ws != nullptr && cudaFreeAsync(ws, s) != cudaSuccess && st == MB200_OK) st = MB200_ERR_CUDA;
+  return st;
 }
+
+MB200_API void mb200_set_sequence_pieces(int pieces) { set_forced_pieces(pieces); }
+
+MB200_API int mb200_sequence_pieces(int64_t ctas, int nchunks) { return seq_pieces(ctas, nchunks); }
 
 MB200_API size_t mb200_selective_scan_bwd_workspace_size(const mb200_scan_bwd_params* p) {
   ScanArgs f;

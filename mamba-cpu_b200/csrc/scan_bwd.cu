@@ -30,6 +30,8 @@
 // delta / dout / z items are prefetched one chunk ahead into registers.
 #include <cooperative_groups.h>
 
+#include <atomic>
+
 #include "scan.cuh"
 #include "quad.cuh"
 #include "segscan.cuh"
@@ -130,7 +132,7 @@ __device__ __forceinline__ void bwd_chunk(const BwdArgs& a, BwdSmem<TW, kBwdWarp
                                           float Dv, float bias, const TI* urow, const TI* drow, const TI* dorow,
                                           const TI* zrow, float& dDacc, float& dbacc, int& rbuf,
                                           uint32_t tcar, ChunkItems<TI, kChunk / S>& items, bool next_vec,
-                                          cg::cluster_group& cluster) {
+                                          int k_lo, cg::cluster_group& cluster) {
   constexpr int K = kChunk / S;
   const ScanArgs& f = a.f;
   const int64_t L = f.L;
@@ -422,7 +424,7 @@ __device__ __forceinline__ void bwd_chunk(const BwdArgs& a, BwdSmem<TW, kBwdWarp
     }
     tmem_st2(tcar + kColDA + n0, dAc[0], dAc[1]);
   }
-  if (k > 0) load_chunk_items<TI, K, HAS_Z>(items, urow, drow, dorow, zrow, t0 - kChunk, L, next_vec);
+  if (k > k_lo) load_chunk_items<TI, K, HAS_Z>(items, urow, drow, dorow, zrow, t0 - kChunk, L, next_vec);
   // -- sum the chunk's partials over the warps of the CTA. red is rewritten only in the next
   //    chunk, after the cluster barrier below, which every thread reaches after this sum.
   __syncthreads();
@@ -561,8 +563,13 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3) scan_bwd_kernel(const BwdAr
   const int warp = threadIdx.x >> 5;
   const int c = lane / S;
   const int s = lane % S;
+  // blockIdx.x = (piece * slices + slice) * tiles + tile; a cluster's CTAs share piece and slice
   const int64_t tile = blockIdx.x % f.tiles;
-  const int64_t slice = blockIdx.x / f.tiles;
+  const int64_t slice = (blockIdx.x / f.tiles) % (f.batch * f.ngroups);
+  const int piece = (int)(blockIdx.x / f.tiles / (f.batch * f.ngroups));
+  const int k_lo = piece * f.piece_chunks;
+  const int k_hi = min(f.nchunks, k_lo + f.piece_chunks);
+  const int64_t rows = f.batch * f.dim;
   const int64_t b = slice / f.ngroups;
   const int64_t g = slice % f.ngroups;
   const int64_t cluster_idx = tile / CL;
@@ -611,6 +618,19 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3) scan_bwd_kernel(const BwdAr
 #pragma unroll
     for (int n = 0; n < kMaxState; ++n)
       init[n] = (valid && n < N && a.dlast != nullptr) ? a.dlast[row * N + n] : 0.f;
+    // an earlier piece starts from the adjoint the later pieces leave: dlast carried through their
+    // decays plus their adjoints from a zero carry (linear in the carry)
+    if (valid) {
+      for (int q = f.pieces - 1; q > piece; --q) {
+#pragma unroll
+        for (int n = 0; n < kMaxState; ++n) {
+          if (n < N) {
+            const int64_t at = ((int64_t)q * rows + row) * N + n;
+            init[n] = fmaf(a.piece_P[at], init[n], a.piece_G[at]);
+          }
+        }
+      }
+    }
     tmem_st16(tcar, init);
 #pragma unroll
     for (int n = 0; n < kMaxState; ++n) init[n] = 0.f;
@@ -654,22 +674,29 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3) scan_bwd_kernel(const BwdAr
   const int nfull = (vec_io && staged) ? (int)(L / kChunk) : 0;
 
   ChunkItems<TI, K> items;
-  if (f.nchunks > 0)
-    load_chunk_items<TI, K, HAS_Z>(items, urow, drow, dorow, zrow, (int64_t)(f.nchunks - 1) * kChunk + s * K, L,
-                                   f.nchunks - 1 < nfull);
-  // The partial last chunk (and every chunk of an unaligned row) goes first: masked, direct loads.
-  for (int k = f.nchunks - 1; k >= nfull; --k) {
+  if (k_hi > k_lo)
+    load_chunk_items<TI, K, HAS_Z>(items, urow, drow, dorow, zrow, (int64_t)(k_hi - 1) * kChunk + s * K, L,
+                                   k_hi - 1 < nfull);
+  // This CTA's piece of the row: chunks [k_lo, k_hi). The partial last chunk (and every chunk of
+  // an unaligned row) goes first: masked, direct loads.
+  for (int k = k_hi - 1; k >= max(k_lo, nfull); --k) {
     bwd_chunk<TI, TW, S, HAS_Z, false, true>(a, sm, 0, k, row, slice, cluster_idx, cl_c, valid, lane, warp, c, s,
                                              Bbase, Cbase, Dv, bias, urow, drow, dorow, zrow, dDacc, dbacc, rbuf,
-                                             tcar, items, k - 1 < nfull, cluster);
+                                             tcar, items, k - 1 < nfull, k_lo, cluster);
   }
   // Full chunks, last to first: B/C + restart states staged one chunk ahead by the bulk-copy
   // engine; the lane's own items of the next chunk are loaded at the end of the current one (2-byte
   // items) or prefetched into L2 (4-byte items).
-  if (nfull > 0 && warp == 0) issue(nfull - 1, (nfull - 1) & 1);
-  for (int k = nfull - 1; k >= 0; --k) {
+  const int kf = min(k_hi, nfull) - 1;  // the piece's last full chunk
+  if (kf >= k_lo) {
+    if (warp == 0) issue(kf, kf & 1);
+    // With dstate < 16 issue() stores the restart states with plain stores, which the first
+    // chunk reads right away (later chunks' stores are ordered by the barrier ending each chunk).
+    __syncthreads();
+  }
+  for (int k = kf; k >= k_lo; --k) {
     const int buf = k & 1;
-    if (k > 0) {
+    if (k > k_lo) {
       if constexpr (!ChunkItems<TI, K>::kCarry) {
         const int64_t t1 = (int64_t)(k - 1) * kChunk + s * K;
         prefetch_l2(urow + t1);
@@ -679,18 +706,18 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3) scan_bwd_kernel(const BwdAr
       }
       if (warp == 0) issue(k - 1, buf ^ 1);
     }
-    // Uses of bar[buf], from the last chunk downwards: chunk k is use number (nfull-1-k)/2.
-    mbar_wait(&sm.bar[buf], (uint32_t)(((nfull - 1 - k) >> 1) & 1));
+    // Uses of bar[buf], from the piece's last full chunk downwards: chunk k is use number (kf-k)/2.
+    mbar_wait(&sm.bar[buf], (uint32_t)(((kf - k) >> 1) & 1));
     bwd_chunk<TI, TW, S, HAS_Z, true, false>(a, sm, buf, k, row, slice, cluster_idx, cl_c, valid, lane, warp, c, s,
                                              Bbase, Cbase, Dv, bias, urow, drow, dorow, zrow, dDacc, dbacc, rbuf,
-                                             tcar, items, true, cluster);
+                                             tcar, items, true, k_lo, cluster);
     // bwd_chunk ends with a cluster barrier wait after its last shared-memory read of this
     // buffer (and of red), so the next iteration may refill it.
   }
 
   // -- the adjoint entering the first step is the gradient of the initial state (every segment
   //    lane of a channel holds it)
-  if (a.dh_init != nullptr) {
+  if (a.dh_init != nullptr && piece == 0) {
     float ghp[kMaxState];
     tmem_wait_st();
     tmem_ld16(tcar, ghp);
@@ -712,7 +739,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3) scan_bwd_kernel(const BwdAr
       float v = dAp[n];
 #pragma unroll
       for (int off = S / 2; off > 0; off >>= 1) v += __shfl_xor_sync(kFull, v, off, S);
-      if (valid && s == 0 && n < N) a.part_A[row * N + n] = v;
+      if (valid && s == 0 && n < N) a.part_A[((int64_t)piece * rows + row) * N + n] = v;
     }
   }
 #pragma unroll
@@ -721,8 +748,8 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3) scan_bwd_kernel(const BwdAr
     dbacc += __shfl_xor_sync(kFull, dbacc, off, S);
   }
   if (valid && s == 0) {
-    a.part_D[row] = dDacc;
-    a.part_db[row] = dbacc;
+    a.part_D[(int64_t)piece * rows + row] = dDacc;
+    a.part_db[(int64_t)piece * rows + row] = dbacc;
   }
   // Peers may still be reading this CTA's red_out through distributed shared memory.
   tmem_fence_before_sync();
@@ -745,7 +772,7 @@ cudaError_t launch_typed(BwdArgs a, int cluster, cudaStream_t stream) {
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(a.f.tiles * a.f.batch * a.f.ngroups));
+  cfg.gridDim = dim3((unsigned)(a.f.tiles * a.f.batch * a.f.ngroups * a.f.pieces));
   cfg.blockDim = dim3(kBwdWarps * 32);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
@@ -761,7 +788,7 @@ cudaError_t launch_typed(BwdArgs a, int cluster, cudaStream_t stream) {
 
 template <typename TI, typename TW>
 cudaError_t launch_seg(const BwdArgs& a, int cluster, cudaStream_t stream) {
-  if (bwd_segments(a.f.batch * a.f.dim) == 8) return launch_typed<TI, TW, 8>(a, cluster, stream);
+  if (bwd_segments(a.f.batch * a.f.dim, a.f.nchunks) == 8) return launch_typed<TI, TW, 8>(a, cluster, stream);
   return launch_typed<TI, TW, 16>(a, cluster, stream);
 }
 
@@ -802,14 +829,14 @@ __global__ void scan_bwd_reduce_kernel(const BwdArgs a, TO* dB, TO* dC, int64_t 
     } else if (i < n_bc4 + n_A) {
       const int64_t j = i - n_bc4;  // d * N + n
       float acc = 0.f;
-      for (int64_t bb = 0; bb < a.f.batch; ++bb) acc += a.part_A[bb * a.f.dim * N + j];
+      for (int64_t pb = 0; pb < a.f.batch * a.f.pieces; ++pb) acc += a.part_A[pb * a.f.dim * N + j];
       dA[j] = acc;
     } else {
       const int64_t dd = i - n_bc4 - n_A;
       float accD = 0.f, accb = 0.f;
-      for (int64_t bb = 0; bb < a.f.batch; ++bb) {
-        accD += a.part_D[bb * a.f.dim + dd];
-        accb += a.part_db[bb * a.f.dim + dd];
+      for (int64_t pb = 0; pb < a.f.batch * a.f.pieces; ++pb) {  // (piece, batch) partials
+        accD += a.part_D[pb * a.f.dim + dd];
+        accb += a.part_db[pb * a.f.dim + dd];
       }
       if (dD) dD[dd] = accD;
       if (db) db[dd] = accb;
@@ -819,9 +846,47 @@ __global__ void scan_bwd_reduce_kernel(const BwdArgs a, TO* dB, TO* dC, int64_t 
 
 }  // namespace
 
-int bwd_segments(int64_t rows) { return rows >= 4096 ? 8 : 16; }
+int bwd_segments(int64_t rows, int nchunks) {
+  // 16 segments per channel (2 channels per warp) give short rows of small problems more warps;
+  // long rows (64 chunks and more) keep 8 and are split into sequence pieces when they are few.
+  return rows >= 4096 || nchunks >= 64 ? 8 : 16;
+}
 
 cudaError_t read_fault_bwd(int* out) { return read_fault_word(out); }
+
+int sm_count() {
+  static std::atomic<int> sms{0};
+  int v = sms.load();
+  if (v == 0) {
+    int dev = 0, n = 0;
+    v = (cudaGetDevice(&dev) == cudaSuccess &&
+         cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && n > 0)
+            ? n
+            : 148;
+    sms.store(v);
+  }
+  return v;
+}
+
+std::atomic<int> g_forced_pieces{0};
+
+void set_forced_pieces(int n) { g_forced_pieces.store(n > 0 ? n : 0); }
+
+int seq_pieces(int64_t ctas, int nchunks) {
+  // Whole rows when they fill at least three quarters of the resident slots (3 CTAs per SM);
+  // below that, split the sequence so the pieces' CTAs fill them: the split costs a summary pass
+  // (the recurrence alone over all pieces but one), which the fuller GPU more than repays.
+  int G = g_forced_pieces.load();
+  if (G <= 0) {
+    const int64_t slots = (int64_t)sm_count() * 3;
+    if (ctas <= 0 || ctas * 4 >= slots * 3) return 1;
+    G = (int)(slots / ctas);
+    if (G > 8) G = 8;
+    if (G > nchunks / 4) G = nchunks / 4;
+  }
+  if (G > nchunks) G = nchunks;
+  return G < 1 ? 1 : G;
+}
 
 int bwd_cluster_size(int64_t tiles, int64_t slices) {
   // Larger clusters divide the dB/dC partials written per slice (fewer cluster partials for the
@@ -829,18 +894,12 @@ int bwd_cluster_size(int64_t tiles, int64_t slices) {
   // resident CTAs (3 per SM) the grid takes. Measured, backward ms with 1 / 2 / 4 / 8 CTAs per
   // cluster: config 2 (0.86 waves) 0.289 / 0.262 / 0.247 / 0.243; config 5 at L 16384 (1.44
   // waves) 7.42 / 7.27 / 7.12 / 7.65 (L 65536: 28.88 with 2, 28.40 with 4); the config-4 layer
-  // shape (4.6 waves) 2.396 with 2, 2.434 with 4. Hence 8 up to one wave, 4 up to two, else 2.
-  static int sms = 0;
-  if (sms == 0) {
-    int dev = 0, n = 0;
-    if (cudaGetDevice(&dev) == cudaSuccess && cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) ==
-                                                    cudaSuccess && n > 0)
-      sms = n;
-    else
-      sms = 148;
-  }
+  // shape (4.6 waves) 2.396 with 2, 2.434 with 4. Hence 8 up to one wave, 4 up to two, else 2;
+  // one wave of 8-CTA clusters holds at most 48 clusters here (384 CTAs: a cluster stays inside
+  // one GPC), so larger one-wave grids take 4.
+  const int sms = sm_count();
   const int64_t ctas = tiles * slices;
-  const int cap = ctas <= (int64_t)sms * 3 ? kMaxCluster : ctas <= (int64_t)sms * 6 ? 4 : 2;
+  const int cap = ctas <= 384 ? kMaxCluster : ctas <= (int64_t)sms * 6 ? 4 : 2;
   int cl = 1;
   while (cl * 2 <= cap && tiles >= cl * 2) cl *= 2;
   return cl;

@@ -149,8 +149,10 @@ __global__ void __launch_bounds__(kThreads, 3) scan_fwd_kernel(const ScanArgs a)
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int warp = tid >> 5;
+  // blockIdx.x = (piece * slices + slice) * tiles + tile
   const int64_t tile = blockIdx.x % a.tiles;
-  const int64_t slice = blockIdx.x / a.tiles;
+  const int64_t slice = (blockIdx.x / a.tiles) % (a.batch * a.ngroups);
+  const int piece = (int)(blockIdx.x / a.tiles / (a.batch * a.ngroups));
   const int64_t b = slice / a.ngroups;
   const int64_t g = slice % a.ngroups;
   const int64_t c0 = tile * Sh::kCPC;  // first channel (inside the group) of this CTA
@@ -177,9 +179,25 @@ __global__ void __launch_bounds__(kThreads, 3) scan_fwd_kernel(const ScanArgs a)
     Aj[j] = (lvalid && n < N) ? a.A[(d0 + cl) * N + n] : 0.f;
     A2[j] = make_float2(Aj[j] * kLog2e, Aj[j] * kLog2e);
     h[j] = (lvalid && n < N && a.h_init != nullptr) ? a.h_init[(row0 + cl) * N + n] : 0.f;
-    h0[j] = h[j];
     P[j] = make_float2(1.f, 1.f);
   }
+  // A later piece starts from the state the earlier pieces leave: h_init carried through their
+  // decays, plus their end states from zero (the recurrence is affine in its initial state).
+  const int64_t rows = a.batch * a.dim;
+  if (lvalid) {
+    for (int q = 0; q < piece; ++q) {
+#pragma unroll
+      for (int j = 0; j < NS; ++j) {
+        const int n = p + j * Sh::kLPC;
+        if (n < N) {
+          const int64_t at = ((int64_t)q * rows + row0 + cl) * N + n;
+          h[j] = fmaf(a.piece_P[at], h[j], a.piece_e[at]);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < NS; ++j) h0[j] = h[j];
   float2 sd = make_float2(0.f, 0.f);
 
   // ---- row-piece tasks (staging and output): piece i covers channel tc[i], steps 4 * tq[i] + 0..3
@@ -311,11 +329,13 @@ __global__ void __launch_bounds__(kThreads, 3) scan_fwd_kernel(const ScanArgs a)
   };
 
   const int nch = a.nchunks;
-  load_chunk(0);
-  stage_chunk(0);
+  const int k_lo = piece * a.piece_chunks;
+  const int k_hi = min(nch, k_lo + a.piece_chunks);
+  load_chunk(k_lo);
+  stage_chunk(k_lo);
   __syncthreads();
-  for (int k = 0; k < nch; ++k) {
-    if (k + 1 < nch) load_chunk(k + 1);
+  for (int k = k_lo; k < k_hi; ++k) {
+    if (k + 1 < k_hi) load_chunk(k + 1);
     const int64_t t0 = (int64_t)k * kChunk;
     const int lim = (int)(L - t0 < kChunk ? L - t0 : kChunk);
     if (lim == kChunk)
@@ -346,10 +366,10 @@ __global__ void __launch_bounds__(kThreads, 3) scan_fwd_kernel(const ScanArgs a)
     }
     __syncthreads();  // partial sums complete; everyone is done reading this chunk's tiles
     if constexpr (WRITE_OUT) write_out(k);
-    if (k + 1 < nch) stage_chunk(k + 1);
+    if (k + 1 < k_hi) stage_chunk(k + 1);
     __syncthreads();
   }
-  if (a.last_state != nullptr && lvalid) {
+  if (a.last_state != nullptr && lvalid && piece == a.pieces - 1) {
     float* st = a.last_state + (row0 + cl) * N;
 #pragma unroll
     for (int j = 0; j < NS; ++j) {
@@ -375,7 +395,7 @@ template <typename TI, typename TW, int NS>
 cudaError_t launch_typed(ScanArgs a, bool write_out, cudaStream_t stream) {
   constexpr int CPC = FwdShape<NS>::kCPC;
   a.tiles = (int)((a.dpg + CPC - 1) / CPC);
-  const dim3 grid((unsigned)(a.tiles * a.batch * a.ngroups));
+  const dim3 grid((unsigned)(a.tiles * a.batch * a.ngroups * a.pieces));
   if (io_rows_strided(a)) {
     if (!write_out) return launch_one<TI, TW, NS, false, false, true>(a, grid, stream);
     if (a.z != nullptr) return launch_one<TI, TW, NS, true, true, true>(a, grid, stream);
@@ -388,16 +408,22 @@ cudaError_t launch_typed(ScanArgs a, bool write_out, cudaStream_t stream) {
 
 template <typename TI, typename TW>
 cudaError_t launch_ns(const ScanArgs& a, bool write_out, cudaStream_t stream) {
-  if (fwd_states_per_lane(a.batch * a.dim) == 1) return launch_typed<TI, TW, 1>(a, write_out, stream);
+  if (fwd_states_per_lane(a.batch * a.dim, a.nchunks) == 1) return launch_typed<TI, TW, 1>(a, write_out, stream);
   return launch_typed<TI, TW, 2>(a, write_out, stream);
 }
 
 }  // namespace
 
-int fwd_states_per_lane(int64_t rows) {
+int fwd_states_per_lane(int64_t rows, int nchunks) {
   // Two states per lane halve the lanes (and the y partial sums) per channel; one state per lane
-  // doubles the warps, which small problems need to fill 148 SMs.
-  return rows < 4096 ? 1 : 2;
+  // doubles the warps, which short rows of small problems need to fill 148 SMs. Long rows (64
+  // chunks and more) keep two and are split into sequence pieces instead when they are few.
+  return rows < 4096 && nchunks < 64 ? 1 : 2;
+}
+
+int64_t fwd_ctas(const ScanArgs& a) {
+  const int64_t cpc = fwd_states_per_lane(a.batch * a.dim, a.nchunks) == 1 ? FwdShape<1>::kCPC : FwdShape<2>::kCPC;
+  return (a.dpg + cpc - 1) / cpc * a.batch * a.ngroups;
 }
 
 cudaError_t read_fault_fwd(int* out) {
@@ -405,9 +431,9 @@ cudaError_t read_fault_fwd(int* out) {
   return cudaSuccess;
 }
 
-cudaError_t launch_scan_fwd(const ScanArgs& a, int io_dtype, int bc_dtype, bool write_out,
-                            cudaStream_t stream) {
-  if (a.batch == 0 || a.dim == 0) return cudaSuccess;
+namespace {
+
+cudaError_t launch_dtypes(const ScanArgs& a, int io_dtype, int bc_dtype, bool write_out, cudaStream_t stream) {
   if (io_dtype == MB200_F32) return launch_ns<float, float>(a, write_out, stream);
   if (io_dtype == MB200_BF16) {
     if (bc_dtype == MB200_BF16) return launch_ns<__nv_bfloat16, __nv_bfloat16>(a, write_out, stream);
@@ -415,6 +441,18 @@ cudaError_t launch_scan_fwd(const ScanArgs& a, int io_dtype, int bc_dtype, bool 
   }
   if (bc_dtype == MB200_F16) return launch_ns<__half, __half>(a, write_out, stream);
   return launch_ns<__half, float>(a, write_out, stream);
+}
+
+}  // namespace
+
+cudaError_t launch_scan_fwd(const ScanArgs& a, int io_dtype, int bc_dtype, bool write_out,
+                            cudaStream_t stream) {
+  if (a.batch == 0 || a.dim == 0) return cudaSuccess;
+  if (a.pieces > 1) {  // summaries of pieces 0 .. pieces - 2, which the pieces after them start from
+    const cudaError_t e = launch_fwd_piece_summary(a, io_dtype, bc_dtype, stream);
+    if (e != cudaSuccess) return e;
+  }
+  return launch_dtypes(a, io_dtype, bc_dtype, write_out, stream);
 }
 
 }  // namespace mb200

@@ -94,6 +94,10 @@ class Conv1dUpdateParams(ctypes.Structure):
 # Every entry point of include/mamba_b200.h with its ctypes signature.
 SIGNATURES = {
     "mb200_selective_scan_fwd": ([ctypes.POINTER(ScanFwdParams), _vp], ctypes.c_int),
+    "mb200_selective_scan_fwd_workspace_size": ([ctypes.POINTER(ScanFwdParams)], ctypes.c_size_t),
+    "mb200_selective_scan_fwd_ws": ([ctypes.POINTER(ScanFwdParams), _vp, ctypes.c_size_t, _vp], ctypes.c_int),
+    "mb200_set_sequence_pieces": ([ctypes.c_int], None),
+    "mb200_sequence_pieces": ([_i64, ctypes.c_int], ctypes.c_int),
     "mb200_selective_scan_bwd_workspace_size": ([ctypes.POINTER(ScanBwdParams)], ctypes.c_size_t),
     "mb200_selective_scan_bwd": ([ctypes.POINTER(ScanBwdParams), _vp, ctypes.c_size_t, _vp], ctypes.c_int),
     "mb200_selective_scan_bwd_noalloc": ([ctypes.POINTER(ScanBwdParams), _vp], ctypes.c_int),
@@ -133,6 +137,12 @@ def _load():
 
 
 lib = _load()
+
+
+def set_sequence_pieces(pieces: int) -> None:
+    """Force the number of sequence pieces per row of the scan kernels (0: automatic, the default).
+    The automatic choice splits rows only when whole rows leave most of the GPU idle."""
+    lib.mb200_set_sequence_pieces(int(pieces))
 
 
 def status_string(status: int) -> str:

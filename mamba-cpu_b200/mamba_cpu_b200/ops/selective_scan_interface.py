@@ -116,7 +116,10 @@ def _run_fwd(name, u, delta, A, B, C, D, z, delta_bias, delta_softplus, initial_
     p.out, p.last_state, p.chunk_states = _lib.ptr(out), _lib.ptr(last_state), _lib.ptr(chunk_states)
     p.initial_state = _lib.ptr(initial_state)
     with torch.cuda.device(u.device):
-        st = _lib.lib.mb200_selective_scan_fwd(p, _lib.stream_of(u))
+        # workspace: the sequence-piece summaries, when rows are split over CTAs (small grids)
+        nbytes = _lib.lib.mb200_selective_scan_fwd_workspace_size(p)
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=u.device) if nbytes else None
+        st = _lib.lib.mb200_selective_scan_fwd_ws(p, _lib.ptr(ws), nbytes, _lib.stream_of(u))
     _lib.check(st, name)
     return out, last_state, chunk_states
 
