@@ -170,10 +170,12 @@ MB200_API int mb200_selective_scan_fwd_ws(const mb200_scan_fwd_params* p, void* 
 /* Force the pieces per row of later calls (0 restores the automatic choice). Process-wide; meant
  * for tests and tuning. */
 MB200_API void mb200_set_sequence_pieces(int pieces);
-/* The automatic choice for a grid of `ctas` CTAs over whole rows of `nchunks` chunks (or the forced
- * count): 1 when the CTAs fill at least three quarters of the resident slots (3 per SM), else
- * min(8, slots / ctas, nchunks / 4). */
-MB200_API int mb200_sequence_pieces(int64_t ctas, int nchunks);
+/* The automatic choice (or the forced count) for the forward (backward = 0) or backward kernel
+ * whose whole rows of `nchunks` chunks give `ctas` CTAs: the count G in 1..8 (at least 4 chunks per
+ * piece) minimising (1 + s (G-1)/G) ceil(G w) / (G w), w = ctas / resident slots (3 per SM), s the
+ * summary pass's cost per element relative to the kernel's (0.8 forward, 0.23 backward); a split
+ * must gain 2 %. */
+MB200_API int mb200_sequence_pieces(int64_t ctas, int nchunks, int backward);
 
 /* Bytes of device workspace mb200_selective_scan_bwd needs for these parameters (0 on bad
  * arguments). Depends on shapes and on whether fwd.chunk_states is NULL, not on pointer values. */

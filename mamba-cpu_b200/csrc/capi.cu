@@ -96,8 +96,8 @@ int build_scan_args(const mb200_scan_fwd_params* p, bool need_out, ScanArgs* a) 
 
 // Sequence pieces for a grid whose whole rows give `ctas` CTAs: (pieces, chunks per piece), with
 // no empty piece.
-void piece_split(int64_t ctas, int nchunks, int* pieces, int* piece_chunks) {
-  int G = nchunks > 1 ? seq_pieces(ctas, nchunks) : 1;
+void piece_split(int64_t ctas, int nchunks, bool backward, int* pieces, int* piece_chunks) {
+  int G = nchunks > 1 ? seq_pieces(ctas, nchunks, backward) : 1;
   int pc = G > 1 ? (nchunks + G - 1) / G : nchunks;
   if (G > 1) G = (nchunks + pc - 1) / pc;
   *pieces = G;
@@ -113,7 +113,7 @@ FwdLayout fwd_layout(const ScanArgs& a) {
   FwdLayout w = {};
   w.pieces = 1;
   w.piece_chunks = a.nchunks;
-  if (a.batch > 0 && a.dim > 0) piece_split(fwd_ctas(a), a.nchunks, &w.pieces, &w.piece_chunks);
+  if (a.batch > 0 && a.dim > 0) piece_split(fwd_ctas(a), a.nchunks, false, &w.pieces, &w.piece_chunks);
   const size_t per = sizeof(float) * (size_t)(w.pieces - 1) * a.batch * a.dim * a.N;
   ScanArgs t = a;
   t.pieces = w.pieces;
@@ -144,7 +144,8 @@ BwdLayout bwd_layout(const ScanArgs& f, bool need_states, bool batch_partials) {
   // batch_partials writes the caller's per-batch partial buffers directly: whole rows only
   w.pieces = 1;
   w.piece_chunks = f.nchunks;
-  if (!batch_partials && f.batch > 0 && f.dim > 0) piece_split(tiles * slices, f.nchunks, &w.pieces, &w.piece_chunks);
+  if (!batch_partials && f.batch > 0 && f.dim > 0)
+    piece_split(tiles * slices, f.nchunks, true, &w.pieces, &w.piece_chunks);
   w.cluster = bwd_cluster_size(tiles, slices * w.pieces);
   w.clusters = (tiles + w.cluster - 1) / w.cluster;
   w.Lpad = (int64_t)f.nchunks * kChunk;
@@ -306,7 +307,9 @@ MB200_API int mb200_selective_scan_fwd(const mb200_scan_fwd_params* p, void* str
 
 MB200_API void mb200_set_sequence_pieces(int pieces) { set_forced_pieces(pieces); }
 
-MB200_API int mb200_sequence_pieces(int64_t ctas, int nchunks) { return seq_pieces(ctas, nchunks); }
+MB200_API int mb200_sequence_pieces(int64_t ctas, int nchunks, int backward) {
+  return seq_pieces(ctas, nchunks, backward != 0);
+}
 
 MB200_API size_t mb200_selective_scan_bwd_workspace_size(const mb200_scan_bwd_params* p) {
   ScanArgs f;

@@ -76,10 +76,11 @@ struct BwdArgs {
   float* piece_P;   // (pieces, batch * dim, N); piece 0 unused
 };
 
-// Sequence pieces per row for a kernel whose whole rows give `ctas` CTAs: 1 when they fill most
-// of the SMs' resident slots (3 CTAs per SM), else enough pieces to fill them (at most 8, at
-// least 4 chunks per piece). mb200_set_sequence_pieces forces a count (tests).
-int seq_pieces(int64_t ctas, int nchunks);
+// Sequence pieces per row for a forward / backward kernel whose whole rows give `ctas` CTAs: the
+// count (1 to 8, at least 4 chunks per piece) that minimises the modelled time of the summary
+// pass plus the grid's rounds of resident slots (3 CTAs per SM). mb200_set_sequence_pieces
+// forces a count (tests).
+int seq_pieces(int64_t ctas, int nchunks, bool backward);
 void set_forced_pieces(int n);  // 0: automatic
 int sm_count();
 // CTAs of the forward over whole rows (its per-CTA channel count depends on the lane layout).

@@ -31,6 +31,7 @@
 #include <cooperative_groups.h>
 
 #include <atomic>
+#include <cmath>
 
 #include "scan.cuh"
 #include "quad.cuh"
@@ -872,17 +873,29 @@ std::atomic<int> g_forced_pieces{0};
 
 void set_forced_pieces(int n) { g_forced_pieces.store(n > 0 ? n : 0); }
 
-int seq_pieces(int64_t ctas, int nchunks) {
-  // Whole rows when they fill at least three quarters of the resident slots (3 CTAs per SM);
-  // below that, split the sequence so the pieces' CTAs fill them: the split costs a summary pass
-  // (the recurrence alone over all pieces but one), which the fuller GPU more than repays.
+int seq_pieces(int64_t ctas, int nchunks, bool backward) {
+  // Pieces trade a summary pass over all pieces but one (relative cost s per element: measured
+  // 0.23 of the backward kernel's, 0.8 of the forward's, whose recurrence is most of its work)
+  // against the idle share of the resident slots (3 CTAs per SM) in the grid's last round:
+  //   cost(G) = (1 + s (G - 1) / G) * ceil(G w) / (G w),   w = CTAs of whole rows / slots,
+  // which also charges grids under one round for their empty slots. G runs from 1 to 8 with at
+  // least 4 chunks per piece. (Config 5 on one GPU: the backward takes 2 pieces, 28.2 -> 25.9 ms,
+  // the forward none; one rank's shard at 8 ranks: 5 pieces both.)
   int G = g_forced_pieces.load();
   if (G <= 0) {
-    const int64_t slots = (int64_t)sm_count() * 3;
-    if (ctas <= 0 || ctas * 4 >= slots * 3) return 1;
-    G = (int)(slots / ctas);
-    if (G > 8) G = 8;
-    if (G > nchunks / 4) G = nchunks / 4;
+    if (ctas <= 0 || nchunks < 2) return 1;
+    const double s = backward ? 0.23 : 0.8;
+    const double w = (double)ctas / ((double)sm_count() * 3);
+    double best = 0.0;
+    G = 1;
+    for (int c = 1; c <= 8 && (c == 1 || c <= nchunks / 4); ++c) {
+      const double fill = c * w;
+      const double cost = (1.0 + s * (c - 1) / c) * std::ceil(fill) / fill;
+      if (c == 1 || cost < best * 0.98) {  // a split must gain at least 2 %
+        best = cost;
+        G = c;
+      }
+    }
   }
   if (G > nchunks) G = nchunks;
   return G < 1 ? 1 : G;

@@ -97,7 +97,7 @@ SIGNATURES = {
     "mb200_selective_scan_fwd_workspace_size": ([ctypes.POINTER(ScanFwdParams)], ctypes.c_size_t),
     "mb200_selective_scan_fwd_ws": ([ctypes.POINTER(ScanFwdParams), _vp, ctypes.c_size_t, _vp], ctypes.c_int),
     "mb200_set_sequence_pieces": ([ctypes.c_int], None),
-    "mb200_sequence_pieces": ([_i64, ctypes.c_int], ctypes.c_int),
+    "mb200_sequence_pieces": ([_i64, ctypes.c_int, ctypes.c_int], ctypes.c_int),
     "mb200_selective_scan_bwd_workspace_size": ([ctypes.POINTER(ScanBwdParams)], ctypes.c_size_t),
     "mb200_selective_scan_bwd": ([ctypes.POINTER(ScanBwdParams), _vp, ctypes.c_size_t, _vp], ctypes.c_int),
     "mb200_selective_scan_bwd_noalloc": ([ctypes.POINTER(ScanBwdParams), _vp], ctypes.c_int),

@@ -19,26 +19,26 @@ from mamba_cpu_b200 import _lib
 
 
 def test_automatic_piece_count():
-    """1 while the CTAs fill three quarters of the slots; else min(8, slots / CTAs, chunks / 4)."""
+    """The modelled-cost choice: (1 + s (G-1)/G) ceil(G w) / (G w) over G = 1..8, w = CTAs / slots,
+    s = 0.8 (forward) / 0.23 (backward), at least 4 chunks per piece, a split gaining 2 %."""
     if torch.cuda.is_available():
         pytest.skip("the rule's slot count comes from the GPU here")
     pieces = _lib.lib.mb200_sequence_pieces
-    assert pieces(640, 1024) == 1      # config 5 on one GPU (1.44 waves)
-    assert pieces(384, 16) == 1        # config 2 (0.86 waves)
-    assert pieces(320, 1024) == 1      # 2 ranks: 0.72 waves -> slots / CTAs = 1
-    assert pieces(160, 1024) == 2      # 4 ranks
-    assert pieces(80, 1024) == 5       # 8 ranks
-    assert pieces(10, 1024) == 8       # at most 8
-    assert pieces(10, 12) == 3         # at least 4 chunks per piece
-    assert pieces(10, 3) == 1
-    assert pieces(0, 100) == 1
+    # config 5 on one GPU (640 CTAs, 1.44 rounds of the 444 slots): the backward splits in two
+    assert (pieces(640, 1024, 0), pieces(640, 1024, 1)) == (1, 2)
+    assert (pieces(384, 16, 0), pieces(384, 16, 1)) == (1, 1)      # config 2 (0.86 rounds)
+    assert (pieces(80, 1024, 0), pieces(80, 1024, 1)) == (5, 5)    # one rank's shard at 8 ranks
+    assert pieces(10, 1024, 1) == 8                                # at most 8
+    assert pieces(10, 12, 1) == 3                                  # at least 4 chunks per piece
+    assert pieces(10, 3, 1) == 1
+    assert pieces(0, 100, 1) == 1
     _lib.set_sequence_pieces(3)
     try:
-        assert pieces(640, 1024) == 3  # forced
-        assert pieces(640, 2) == 2     # never more pieces than chunks
+        assert pieces(640, 1024, 0) == 3  # forced
+        assert pieces(640, 2, 1) == 2     # never more pieces than chunks
     finally:
         _lib.set_sequence_pieces(0)
-    assert pieces(640, 1024) == 1
+    assert pieces(640, 1024, 0) == 1
 
 
 # ---------------------------------------------------------------------------------------------
@@ -180,7 +180,7 @@ def test_automatic_pieces_on_a_rank_shard():
 
     b, d, l, n = 2, 640, 4096, 16
     ctas = b * (d // 16)
-    assert _lib.lib.mb200_sequence_pieces(ctas, l // 64) > 1
+    assert _lib.lib.mb200_sequence_pieces(ctas, l // 64, 0) > 1 and _lib.lib.mb200_sequence_pieces(ctas, l // 64, 1) > 1
     inp = make_inputs(b, d, l, n, 1, True, True, False, torch.bfloat16, a_scale=15.5)
     dout = torch.randn(b, d, l, generator=torch.Generator().manual_seed(2)).to(torch.bfloat16).cuda()
     res = []
