@@ -745,7 +745,9 @@ def run_ours(args):
         "ms_fwd": dtm["ms_fwd"],
         "ms_bwd": dtm["ms_bwd"],
         "hbm_frac_step": (fwd_bytes + bwd_bytes) / (ms_step * 1e-3) / 1e9 / peak,
-        "roofline": roofline_block("backward", "scan_bwd_kernel + scan_bwd_reduce_kernel (the backward op, per rank)",
+        "roofline": roofline_block("backward", "the backward op, per rank: scan_bwd_kernel + scan_bwd_reduce_kernel "
+                                   "(+ scan_piece_summary_kernel and piece_combine_kernel when rows are split "
+                                   "into sequence pieces)",
                                    bwd_bytes, dtm["ms_bwd"], peak, peak_kind, traffic.get("bwd_bytes_per_element"),
                                    E_rank),
         "roofline_fwd": roofline_block("forward", "scan_fwd_kernel (per rank)", fwd_bytes, dtm["ms_fwd"], peak,
