@@ -907,7 +907,8 @@ int bwd_cluster_size(int64_t tiles, int64_t slices) {
   // resident CTAs (3 per SM) the grid takes. Measured, backward ms with 1 / 2 / 4 / 8 CTAs per
   // cluster: config 2 (0.86 waves) 0.289 / 0.262 / 0.247 / 0.243; config 5 at L 16384 (1.44
   // waves) 7.42 / 7.27 / 7.12 / 7.65 (L 65536: 28.88 with 2, 28.40 with 4); the config-4 layer
-  // shape (4.6 waves) 2.396 with 2, 2.434 with 4. Hence 8 up to one wave, 4 up to two, else 2;
+  // shape (4.6 waves) 2.396 with 2, 2.434 with 4; config 5 in 2 sequence pieces (2.9 waves) 25.9
+  // with 2, 30.7 with 4. Hence 8 up to one wave, 4 up to two, else 2;
   // one wave of 8-CTA clusters holds at most 48 clusters here (384 CTAs: a cluster stays inside
   // one GPC), so larger one-wave grids take 4.
   const int sms = sm_count();
