@@ -133,7 +133,7 @@ __device__ __forceinline__ void bwd_chunk(const BwdArgs& a, BwdSmem<TW, kBwdWarp
                                           float Dv, float bias, const TI* urow, const TI* drow, const TI* dorow,
                                           const TI* zrow, float& dDacc, float& dbacc, int& rbuf,
                                           uint32_t tcar, ChunkItems<TI, kChunk / S>& items, bool next_vec,
-                                          int k_lo, cg::cluster_group& cluster) {
+                                          cg::cluster_group& cluster) {
   constexpr int K = kChunk / S;
   const ScanArgs& f = a.f;
   const int64_t L = f.L;
@@ -425,7 +425,9 @@ __device__ __forceinline__ void bwd_chunk(const BwdArgs& a, BwdSmem<TW, kBwdWarp
     }
     tmem_st2(tcar + kColDA + n0, dAc[0], dAc[1]);
   }
-  if (k > k_lo) load_chunk_items<TI, K, HAS_Z>(items, urow, drow, dorow, zrow, t0 - kChunk, L, next_vec);
+  // (the first chunk of a later sequence piece loads the chunk before it for nothing: in bounds,
+  // and cheaper than another live value in this loop)
+  if (k > 0) load_chunk_items<TI, K, HAS_Z>(items, urow, drow, dorow, zrow, t0 - kChunk, L, next_vec);
   // -- sum the chunk's partials over the warps of the CTA. red is rewritten only in the next
   //    chunk, after the cluster barrier below, which every thread reaches after this sum.
   __syncthreads();
@@ -683,7 +685,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3) scan_bwd_kernel(const BwdAr
   for (int k = k_hi - 1; k >= max(k_lo, nfull); --k) {
     bwd_chunk<TI, TW, S, HAS_Z, false, true>(a, sm, 0, k, row, slice, cluster_idx, cl_c, valid, lane, warp, c, s,
                                              Bbase, Cbase, Dv, bias, urow, drow, dorow, zrow, dDacc, dbacc, rbuf,
-                                             tcar, items, k - 1 < nfull, k_lo, cluster);
+                                             tcar, items, k - 1 < nfull, cluster);
   }
   // Full chunks, last to first: B/C + restart states staged one chunk ahead by the bulk-copy
   // engine; the lane's own items of the next chunk are loaded at the end of the current one (2-byte
@@ -692,8 +694,9 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3) scan_bwd_kernel(const BwdAr
   if (kf >= k_lo) {
     if (warp == 0) issue(kf, kf & 1);
     // With dstate < 16 issue() stores the restart states with plain stores, which the first
-    // chunk reads right away (later chunks' stores are ordered by the barrier ending each chunk).
-    __syncthreads();
+    // chunk reads right away (later chunks' stores are ordered by the barrier ending each chunk;
+    // with dstate 16 they come by bulk copy, ordered by the mbarrier).
+    if (N != kMaxState) __syncthreads();
   }
   for (int k = kf; k >= k_lo; --k) {
     const int buf = k & 1;
@@ -711,7 +714,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3) scan_bwd_kernel(const BwdAr
     mbar_wait(&sm.bar[buf], (uint32_t)(((kf - k) >> 1) & 1));
     bwd_chunk<TI, TW, S, HAS_Z, true, false>(a, sm, buf, k, row, slice, cluster_idx, cl_c, valid, lane, warp, c, s,
                                              Bbase, Cbase, Dv, bias, urow, drow, dorow, zrow, dDacc, dbacc, rbuf,
-                                             tcar, items, true, k_lo, cluster);
+                                             tcar, items, true, cluster);
     // bwd_chunk ends with a cluster barrier wait after its last shared-memory read of this
     // buffer (and of red), so the next iteration may refill it.
   }
