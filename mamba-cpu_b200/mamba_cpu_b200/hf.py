@@ -67,10 +67,11 @@ def mamba_inner_fn(xz, conv1d_weight, conv1d_bias, x_proj_weight, delta_proj_wei
     x = causal_conv1d_fn(x, conv1d_weight.reshape(conv1d_weight.shape[0], -1), conv1d_bias, activation="silu")
     d_inner = x.shape[1]
     x_dbl = F.linear(x.transpose(1, 2).reshape(batch * seqlen, d_inner), x_proj_weight)  # (b l, r + 2n)
-    delta = F.linear(x_dbl[:, :dt_rank], delta_proj_weight)  # (b l, d)
+    # delta as (d, b l): its (b, d, l) view below is seqlen-contiguous, which the scan reads in place
+    delta = delta_proj_weight @ x_dbl[:, :dt_rank].t()
     if dt_rms_weight is not None:
-        delta = _rms_norm(delta, dt_rms_weight, b_c_dt_rms_eps)
-    delta = delta.reshape(batch, seqlen, d_inner).transpose(1, 2)  # (b, d, l)
+        delta = _rms_norm(delta.t(), dt_rms_weight, b_c_dt_rms_eps).t()  # over d_inner
+    delta = delta.reshape(d_inner, batch, seqlen).transpose(0, 1)  # (b, d, l)
 
     def _bc(M, start, bias, rms_w):
         if M is not None:

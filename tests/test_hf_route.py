@@ -135,9 +135,11 @@ def test_mamba_inner_fn_composition(falcon, monkeypatch):
     for fn in (hf.mamba_inner_fn, inner_fn_ref):
         out = fn(*args, **kw)
         outs.append((out.detach(), torch.autograd.grad((out * out.detach().cos()).sum(), leaves)))
-    torch.testing.assert_close(outs[0][0], outs[1][0], rtol=1e-12, atol=1e-12)
+    # the two compositions associate the projections' float64 sums differently, and the reference
+    # ops compute in float32 inside, so a last-bit difference can flip a float32 rounding
+    torch.testing.assert_close(outs[0][0], outs[1][0], rtol=1e-6, atol=1e-8)
     for ga, gb in zip(outs[0][1], outs[1][1]):
-        torch.testing.assert_close(ga, gb, rtol=1e-10, atol=1e-12)
+        torch.testing.assert_close(ga, gb, rtol=1e-5, atol=1e-8)
 
 
 def _model():
