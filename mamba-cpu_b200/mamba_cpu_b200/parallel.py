@@ -262,14 +262,26 @@ def _use_peer_sum(group, t: torch.Tensor) -> bool:
     return world > 1 and int(os.environ.get("LOCAL_WORLD_SIZE", str(world))) >= world
 
 
+# Largest [dB | dC] exchange (bytes) the one-shot peer-memory sum takes; larger ones go to one
+# NCCL all_reduce. Measured on 2 B200s: 13.7 / 15.1 us (peer / NCCL) at 0.5 MB, 108 / 65 us at
+# 16.8 MB -- the one-shot sum reads every peer's whole buffer, NCCL's reduce-scatter + all-gather
+# moves about twice the buffer whatever the rank count -- crossing near 1 MB.
+PEER_MAX_BYTES_DEFAULT = 1 << 20
+
+
 def all_reduce_bc(dB: torch.Tensor, dC: torch.Tensor, group, async_op: bool = False):
     """Sum the fp32 partial dB / dC over the shards of ``group`` in ONE exchange and return the
-    sums. For node-local NCCL groups this is a one-shot sum over NVLink peer memory
-    (:class:`PeerReducer`) that overwrites dB and dC in place; otherwise one ``all_reduce`` of
-    their concatenation."""
+    sums. For node-local NCCL groups and exchanges up to MAMBA_B200_PEER_REDUCE_MAX_BYTES (1 MiB)
+    this is a one-shot sum over NVLink peer memory (:class:`PeerReducer`) that overwrites dB and dC
+    in place (ranks added in rank order); otherwise one ``all_reduce`` of their concatenation,
+    whose sums are returned as views of the concatenated buffer."""
+    import os
+
     import torch.distributed as dist
 
-    if (_use_peer_sum(group, dB) and dB.dtype == dC.dtype == torch.float32
+    nbytes = (dB.numel() + dC.numel()) * 4
+    small = nbytes <= int(os.environ.get("MAMBA_B200_PEER_REDUCE_MAX_BYTES", str(PEER_MAX_BYTES_DEFAULT)))
+    if (small and _use_peer_sum(group, dB) and dB.dtype == dC.dtype == torch.float32
             and dB.is_contiguous() and dC.is_contiguous()):
         key = (id(group), dB.numel(), dC.numel())
         if key not in _reducers:  # None: the peer exchange is unavailable for this group (NCCL)
