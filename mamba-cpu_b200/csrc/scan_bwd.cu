@@ -567,9 +567,10 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3) scan_bwd_kernel(const BwdAr
   const int c = lane / S;
   const int s = lane % S;
   // blockIdx.x = (piece * slices + slice) * tiles + tile; a cluster's CTAs share piece and slice
-  const int64_t tile = blockIdx.x % f.tiles;
-  const int64_t slice = (blockIdx.x / f.tiles) % (f.batch * f.ngroups);
-  const int piece = (int)(blockIdx.x / f.tiles / (f.batch * f.ngroups));
+  const unsigned bx = blockIdx.x, ntiles = (unsigned)f.tiles, nslices = (unsigned)(f.batch * f.ngroups);
+  const int64_t tile = bx % ntiles;  // 32-bit index arithmetic: grids stay below 2^31 CTAs
+  const int64_t slice = (bx / ntiles) % nslices;
+  const int piece = (int)(bx / ntiles / nslices);
   const int k_lo = piece * f.piece_chunks;
   const int k_hi = min(f.nchunks, k_lo + f.piece_chunks);
   const int64_t rows = f.batch * f.dim;

@@ -150,9 +150,10 @@ __global__ void __launch_bounds__(kThreads, 3) scan_fwd_kernel(const ScanArgs a)
   const int lane = tid & 31;
   const int warp = tid >> 5;
   // blockIdx.x = (piece * slices + slice) * tiles + tile
-  const int64_t tile = blockIdx.x % a.tiles;
-  const int64_t slice = (blockIdx.x / a.tiles) % (a.batch * a.ngroups);
-  const int piece = (int)(blockIdx.x / a.tiles / (a.batch * a.ngroups));
+  const unsigned bx = blockIdx.x, ntiles = (unsigned)a.tiles, nslices = (unsigned)(a.batch * a.ngroups);
+  const int64_t tile = bx % ntiles;  // 32-bit index arithmetic: grids stay below 2^31 CTAs
+  const int64_t slice = (bx / ntiles) % nslices;
+  const int piece = (int)(bx / ntiles / nslices);
   const int64_t b = slice / a.ngroups;
   const int64_t g = slice % a.ngroups;
   const int64_t c0 = tile * Sh::kCPC;  // first channel (inside the group) of this CTA
