@@ -194,3 +194,38 @@ def test_automatic_pieces_on_a_rank_shard():
     for a, c in zip(res[0], res[1]):
         sc = max(1.0, float(c.abs().max()))
         torch.testing.assert_close(a / sc, c / sc, rtol=2e-2, atol=2e-2)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("seed", range(6))
+def test_random_shapes_and_piece_counts(seed):
+    """Random small problems (batch, dim, seqlen, dstate, groups, gate, bias, softplus, dtype) with
+    a random forced piece count: split rows agree with whole rows (fp32 to 1e-5 relative of each
+    tensor's largest value, bf16 to 2e-2)."""
+    import random
+
+    import mamba_cpu_b200 as mb
+    from helpers import make_inputs, to_cuda
+
+    rnd = random.Random(seed)
+    b, d = rnd.choice([1, 2, 3]), rnd.choice([8, 24, 40])
+    L = rnd.randint(65, 64 * 12 + 40)
+    n = rnd.choice([4, 13, 16])
+    g = rnd.choice([None, 1, 2]) if d % 2 == 0 else None
+    has_z, has_bias, softplus = rnd.random() < 0.5, rnd.random() < 0.5, rnd.random() < 0.7
+    dtype = rnd.choice([torch.float32, torch.bfloat16])
+    pieces = rnd.randint(2, 8)
+    inp = make_inputs(b, d, L, n, g, True, has_z, has_bias, dtype, seed=seed, a_scale=4.0)
+    dout = torch.randn(b, d, L, generator=torch.Generator().manual_seed(seed)).to(dtype).cuda()
+    res = []
+    for pc in (1, pieces):
+        leaves = to_cuda(inp, requires_grad=True)
+        with _Pieces(pc):
+            out, last = mb.selective_scan_fn(**leaves, delta_softplus=softplus, return_last_state=True)
+            (out.float() * dout.float()).sum().add(last.sum()).backward()
+        torch.cuda.synchronize()
+        res.append([out.detach().float(), last.detach()] + [leaves[k].grad.float() for k in KEYS if leaves[k] is not None])
+    tol = 1e-5 if dtype == torch.float32 else 2e-2
+    for a, c in zip(res[0], res[1]):
+        sc = max(1.0, float(a.abs().max()))
+        torch.testing.assert_close(c / sc, a / sc, rtol=tol, atol=tol)
