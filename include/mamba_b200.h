@@ -311,6 +311,58 @@ typedef struct mb200_conv1d_update_params {
 
 MB200_API int mb200_causal_conv1d_update(const mb200_conv1d_update_params* p, void* stream);
 
+/* ---- Mamba-2 SSD chunk scan (forward) ------------------------------------------------------
+ *
+ * The reference lists the Mamba-2 SSD scan `mamba_chunk_scan_combined` as a roadmap item
+ * (README.md:94) and has no implementation of it; this entry point computes the forward of
+ * upstream mamba_ssm's function of that name (ssd_combined.py). Per (batch, head), with a scalar
+ * decay A[h] shared by the head's headdim x dstate state:
+ *   dt_t  = clamp(softplus?(dt[b, t, h] + dt_bias[h]), dt_min, dt_max)
+ *   h_t   = exp(dt_t A[h]) h_{t-1} + dt_t x_t B_t^T        (headdim x dstate, fp32)
+ *   y_t   = h_t C_t + D x_t ;   out_t = y_t * silu(z_t) when z is given
+ * which is the Mamba-1 selective scan with channels = nheads * headdim, A broadcast over dstate
+ * and delta broadcast over headdim (the reference's selective_scan_fwd_f32 on those inputs,
+ * csrc/selective_scan.cpp:120-145, computes the same values).
+ *   x, z, out       : (batch, seqlen, nheads, headdim) bf16; headdim contiguous, other strides
+ *                     below (out dense). Row starts (x, z, out, B, C) 16-byte aligned.
+ *   dt              : (batch, seqlen, nheads) float32, nheads contiguous, strides below
+ *   A               : (nheads) float32; dt_bias (nheads) float32 or NULL
+ *   B, C            : (batch, seqlen, ngroups, dstate) bf16, dstate contiguous; head h reads
+ *                     group h / (nheads / ngroups)
+ *   D               : (nheads) or (nheads, headdim) (D_per_dim = 1) float32, or NULL
+ *   initial_states  : (batch, nheads, headdim, dstate) float32 or NULL (zeros)
+ *   final_states    : (batch, nheads, headdim, dstate) float32 or NULL: the state after the last
+ *                     step
+ * Limits of this build: x_dtype MB200_BF16, dstate a multiple of 8 up to 128, headdim a multiple
+ * of 32 up to 256 (MB200_ERR_UNSUPPORTED otherwise). One kernel launch, no scratch memory.
+ */
+typedef struct mb200_ssd_params {
+  const void* x;
+  const float* dt;
+  const float* A;
+  const void* B;
+  const void* C;
+  const float* D;
+  const void* z;
+  const float* dt_bias;
+  const float* initial_states;
+  void* out;
+  float* final_states;
+  int64_t batch, seqlen, nheads, headdim, ngroups, dstate;
+  int64_t x_batch_stride, x_seqlen_stride, x_head_stride;
+  int64_t z_batch_stride, z_seqlen_stride, z_head_stride;
+  int64_t B_batch_stride, B_seqlen_stride, B_group_stride;
+  int64_t C_batch_stride, C_seqlen_stride, C_group_stride;
+  int64_t dt_batch_stride, dt_seqlen_stride;
+  float dt_min, dt_max;
+  int32_t x_dtype;
+  int32_t dt_softplus;
+  int32_t D_per_dim;
+  int32_t reserved;
+} mb200_ssd_params;
+
+MB200_API int mb200_ssd_chunk_scan_fwd(const mb200_ssd_params* p, void* stream);
+
 /* ---- misc -------------------------------------------------------------------------------- */
 
 /* ---- one-shot sum over the GPUs of a node through peer memory ------------------------------

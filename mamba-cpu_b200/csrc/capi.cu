@@ -558,10 +558,11 @@ MB200_API int mb200_last_launch_count(void) { return g_launches; }
 
 MB200_API int mb200_device_fault(int* fault) {
   if (fault == nullptr) return MB200_ERR_NULL_POINTER;
-  int f0 = 0, f1 = 0, f2 = 0;
-  if (read_fault_fwd(&f0) != cudaSuccess || read_fault_bwd(&f1) != cudaSuccess || read_fault_peer(&f2) != cudaSuccess)
+  int f0 = 0, f1 = 0, f2 = 0, f3 = 0;
+  if (read_fault_fwd(&f0) != cudaSuccess || read_fault_bwd(&f1) != cudaSuccess || read_fault_peer(&f2) != cudaSuccess ||
+      read_fault_ssd(&f3) != cudaSuccess)
     return MB200_ERR_CUDA;
-  *fault = f0 | f1 | f2;
+  *fault = f0 | f1 | f2 | f3;
   return MB200_OK;
 }
 

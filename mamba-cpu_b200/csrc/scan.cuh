@@ -93,6 +93,7 @@ int fwd_states_per_lane(int64_t rows, int nchunks);
 cudaError_t read_fault_fwd(int* out);
 cudaError_t read_fault_bwd(int* out);
 cudaError_t read_fault_peer(int* out);
+cudaError_t read_fault_ssd(int* out);
 int bwd_segments(int64_t rows, int nchunks);
 int bwd_cluster_size(int64_t tiles, int64_t slices);
 

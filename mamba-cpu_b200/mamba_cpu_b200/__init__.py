@@ -3,7 +3,8 @@
 The public functions have the signatures of mamba-cpu / mamba_ssm / causal_conv1d
 (mamba-cpu src/mamba_cpu/__init__.py:3-23) and run hand-written CUDA kernels from
 libmamba_b200.so on CUDA tensors. Non-CUDA tensors are rejected, as the reference rejects
-non-CPU ones. ``selective_scan_ref`` and ``causal_conv1d_ref`` are plain PyTorch versions of the
+non-CPU ones. ``mamba_chunk_scan_combined`` adds the Mamba-2 SSD scan forward (a roadmap item of
+the reference) with upstream mamba_ssm's signature. ``selective_scan_ref`` and ``causal_conv1d_ref`` are plain PyTorch versions of the
 two operators (any device), exported as the reference exports its own.
 """
 
@@ -11,6 +12,7 @@ from mamba_cpu_b200 import hf, parallel
 from mamba_cpu_b200.ops import (
     causal_conv1d_fn,
     causal_conv1d_update,
+    mamba_chunk_scan_combined,
     selective_scan_fn,
     selective_state_update,
 )
@@ -23,6 +25,7 @@ __all__ = [
     "causal_conv1d_ref",
     "causal_conv1d_update",
     "hf",
+    "mamba_chunk_scan_combined",
     "parallel",
     "selective_scan_fn",
     "selective_scan_ref",

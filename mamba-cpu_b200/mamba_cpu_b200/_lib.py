@@ -91,6 +91,22 @@ class Conv1dUpdateParams(ctypes.Structure):
     ]
 
 
+class SsdParams(ctypes.Structure):
+    _fields_ = [
+        ("x", _vp), ("dt", _vp), ("A", _vp), ("B", _vp), ("C", _vp), ("D", _vp), ("z", _vp),
+        ("dt_bias", _vp), ("initial_states", _vp), ("out", _vp), ("final_states", _vp),
+        ("batch", _i64), ("seqlen", _i64), ("nheads", _i64), ("headdim", _i64), ("ngroups", _i64),
+        ("dstate", _i64),
+        ("x_batch_stride", _i64), ("x_seqlen_stride", _i64), ("x_head_stride", _i64),
+        ("z_batch_stride", _i64), ("z_seqlen_stride", _i64), ("z_head_stride", _i64),
+        ("B_batch_stride", _i64), ("B_seqlen_stride", _i64), ("B_group_stride", _i64),
+        ("C_batch_stride", _i64), ("C_seqlen_stride", _i64), ("C_group_stride", _i64),
+        ("dt_batch_stride", _i64), ("dt_seqlen_stride", _i64),
+        ("dt_min", ctypes.c_float), ("dt_max", ctypes.c_float),
+        ("x_dtype", _i32), ("dt_softplus", _i32), ("D_per_dim", _i32), ("reserved", _i32),
+    ]
+
+
 # Every entry point of include/mamba_b200.h with its ctypes signature.
 SIGNATURES = {
     "mb200_selective_scan_fwd": ([ctypes.POINTER(ScanFwdParams), _vp], ctypes.c_int),
@@ -109,6 +125,7 @@ SIGNATURES = {
                                  ctypes.c_size_t, _vp], ctypes.c_int),
     "mb200_selective_state_update": ([ctypes.POINTER(StateUpdateParams), _vp], ctypes.c_int),
     "mb200_causal_conv1d_update": ([ctypes.POINTER(Conv1dUpdateParams), _vp], ctypes.c_int),
+    "mb200_ssd_chunk_scan_fwd": ([ctypes.POINTER(SsdParams), _vp], ctypes.c_int),
     "mb200_status_string": ([ctypes.c_int], ctypes.c_char_p),
     "mb200_version": ([], ctypes.c_int),
     "mb200_last_launch_count": ([], ctypes.c_int),

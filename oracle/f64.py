@@ -38,6 +38,9 @@ def _load():
         lib.oracle_state_update.restype = None
         lib.oracle_conv1d_update.argtypes = [_P] * 5 + [_I] * 5 + [ctypes.c_int]
         lib.oracle_conv1d_update.restype = None
+        lib.oracle_ssd_fwd.argtypes = [_P] * 11 + [_I] * 6 + [ctypes.c_int, ctypes.c_double, ctypes.c_double,
+                                                                ctypes.c_int]
+        lib.oracle_ssd_fwd.restype = ctypes.c_int
         lib.oracle_set_num_threads.argtypes = [ctypes.c_int]
         lib.oracle_num_threads.restype = ctypes.c_int
         _lib = lib
@@ -175,3 +178,21 @@ def conv1d_update(x, conv_state, weight, bias=None, activation=None):
                                  _ptr(out), batch, dim, seqlen, st.shape[-1], w.shape[1],
                                  int(activation in ("silu", "swish")))
     return (out[..., 0] if single else out), st
+
+
+def ssd_fwd(x, dt, A, B, C, D=None, z=None, dt_bias=None, initial_states=None, dt_softplus=False,
+            dt_limit=(0.0, float("inf"))):
+    """Mamba-2 SSD scan, step by step in float64. x, z (b, l, h, p); dt (b, l, h); A, dt_bias (h);
+    B, C (b, l, g, n); D (h) or (h, p); initial_states (b, h, p, n). Returns (out, final_states)."""
+    x, dt, A, B, C, D, z, dt_bias, init = map(_f32, (x, dt, A, B, C, D, z, dt_bias, initial_states))
+    batch, seqlen, nheads, headdim = x.shape
+    ngroups, dstate = B.shape[2], B.shape[3]
+    out = np.empty(x.shape, np.float64)
+    fin = np.empty((batch, nheads, headdim, dstate), np.float64)
+    rc = _load().oracle_ssd_fwd(
+        _ptr(x), _ptr(dt), _ptr(A), _ptr(B), _ptr(C), _ptr(D), _ptr(z), _ptr(dt_bias), _ptr(init), _ptr(out),
+        _ptr(fin), batch, seqlen, nheads, headdim, ngroups, dstate, int(bool(dt_softplus)),
+        float(dt_limit[0]), float(dt_limit[1]), int(D is not None and D.ndim == 2))
+    if rc:
+        raise ValueError(f"oracle_ssd_fwd rejected its arguments (status {rc})")
+    return out, fin

@@ -487,3 +487,74 @@ void oracle_conv1d_update(const float* x, double* conv_state, const float* w, co
   free(full);
 }
 
+
+/* ---- Mamba-2 SSD scan (forward) ----------------------------------------------------------
+ * The reference has no SSD implementation (README.md:94 lists it as a roadmap item). This is
+ * the recurrence of upstream mamba_ssm's mamba_chunk_scan_combined stated step by step, which
+ * is the reference's Mamba-1 recurrence (csrc/selective_scan.cpp:120-145) with channels =
+ * nheads * headdim, A[h] shared by all dstate entries and dt[b, t, h] shared by the head's
+ * headdim channels:
+ *   dt_t = clamp(softplus?(dt + dt_bias[h]), dt_min, dt_max)
+ *   s[p][n] = exp(dt_t A[h]) s[p][n] + dt_t x[p] B[n];  y[p] = sum_n s[p][n] C[n] + D x[p];
+ *   out = y * silu(z).
+ * Layouts (dense): x, z, out (b, l, h, p); dt (b, l, h); B, C (b, l, g, n); D (h) or (h, p)
+ * (D_per_dim); initial / final states (b, h, p, n). Head h reads group h / (h_total / g). */
+typedef struct {
+  const float *x, *dt, *A, *B, *C, *D, *z, *dt_bias, *init;
+  double *out, *final_states;
+  int64_t batch, seqlen, nheads, headdim, ngroups, dstate;
+  int softplus, D_per_dim;
+  double dt_min, dt_max;
+} ssd_ctx;
+
+static void ssd_rows(int64_t lo, int64_t hi, void* vctx) {
+  const ssd_ctx* c = (const ssd_ctx*)vctx;
+  const int64_t L = c->seqlen, H = c->nheads, P = c->headdim, G = c->ngroups, N = c->dstate;
+  double* s = (double*)malloc(sizeof(double) * (size_t)(P * N));
+  for (int64_t r = lo; r < hi; ++r) { /* r = b * H + h */
+    const int64_t b = r / H, h = r % H, g = h / (H / G);
+    for (int64_t i = 0; i < P * N; ++i) s[i] = c->init ? (double)c->init[r * P * N + i] : 0.0;
+    const double A = (double)c->A[h];
+    for (int64_t t = 0; t < L; ++t) {
+      double dt = (double)c->dt[(b * L + t) * H + h] + (c->dt_bias ? (double)c->dt_bias[h] : 0.0);
+      if (c->softplus) dt = softplus_d(dt);
+      dt = fmin(fmax(dt, c->dt_min), c->dt_max);
+      const double decay = exp(dt * A);
+      const float* Bt = c->B + ((b * L + t) * G + g) * N;
+      const float* Ct = c->C + ((b * L + t) * G + g) * N;
+      const int64_t row = ((b * L + t) * H + h) * P;
+      for (int64_t p = 0; p < P; ++p) {
+        const double xv = (double)c->x[row + p];
+        double y = 0.0;
+        for (int64_t n = 0; n < N; ++n) {
+          double* sp = &s[p * N + n];
+          *sp = decay * *sp + dt * xv * (double)Bt[n];
+          y += *sp * (double)Ct[n];
+        }
+        if (c->D) y += xv * (double)(c->D_per_dim ? c->D[h * P + p] : c->D[h]);
+        if (c->z) {
+          const double zv = (double)c->z[row + p];
+          y *= zv * sigmoid_d(zv);
+        }
+        c->out[row + p] = y;
+      }
+    }
+    if (c->final_states)
+      for (int64_t i = 0; i < P * N; ++i) c->final_states[r * P * N + i] = s[i];
+  }
+  free(s);
+}
+
+int oracle_ssd_fwd(const float* x, const float* dt, const float* A, const float* B, const float* C,
+                   const float* D, const float* z, const float* dt_bias, const float* init, double* out,
+                   double* final_states, int64_t batch, int64_t seqlen, int64_t nheads, int64_t headdim,
+                   int64_t ngroups, int64_t dstate, int softplus, double dt_min, double dt_max,
+                   int D_per_dim) {
+  if (!x || !dt || !A || !B || !C || !out) return 1;
+  if (batch < 0 || seqlen < 0 || nheads < 0 || headdim <= 0 || ngroups <= 0 || dstate <= 0) return 2;
+  if (nheads % ngroups != 0) return 2;
+  ssd_ctx c = {x, dt, A, B, C, D, z, dt_bias, init, out, final_states, batch, seqlen, nheads, headdim,
+               ngroups, dstate, softplus, D_per_dim, dt_min, dt_max};
+  parallel_for(batch * nheads, ssd_rows, &c);
+  return 0;
+}

@@ -19,6 +19,7 @@ The GPU tests and the float64 oracle are checked against these files; nothing at
 GPU box needs the reference.
 """
 
+import math
 import os
 import sys
 
@@ -252,9 +253,69 @@ def make_state_update(m):
     st.save("state_update.npz")
 
 
+def _bf16_exact(t):
+    """Values representable in bfloat16 (the SSD kernel's input dtype), kept in float32."""
+    return t.to(torch.bfloat16).float()
+
+
+def make_ssd(m):
+    """Mamba-2 SSD cases. The reference has no SSD scan (README.md:94 lists it as a roadmap item), but
+    the SSD recurrence is its Mamba-1 selective scan with channels = nheads * headdim, A[h] repeated
+    over dstate and dt[b, t, h] repeated over headdim, so the reference's own selective_scan_fn (its
+    compiled kernel) produces the outputs and final states recorded here."""
+    st = Store()
+    cases = [
+        # b, l, h, p, g, n, D mode, z, dt_bias, dt regime
+        (1, 200, 2, 32, 1, 16, "h", True, True, "wide"),
+        (2, 200, 2, 64, 2, 64, "hp", False, False, "wide"),
+        (1, 130, 2, 32, 1, 128, None, True, False, "wide"),
+        (2, 257, 2, 32, 2, 8, "h", True, True, "mamba2"),
+        (1, 64, 1, 32, 1, 24, "hp", False, True, "mamba2"),
+        (1, 260, 2, 64, 1, 128, "h", True, True, "mamba2"),
+    ]
+    for seed, (b, l, h, p, g, n, dmode, has_z, has_bias, regime) in enumerate(cases):
+        gen = torch.Generator().manual_seed(100 + seed)
+        x = _bf16_exact(torch.randn(b, l, h, p, generator=gen))
+        B = _bf16_exact(torch.randn(b, l, g, n, generator=gen))
+        C = _bf16_exact(torch.randn(b, l, g, n, generator=gen))
+        z = _bf16_exact(torch.randn(b, l, h, p, generator=gen)) if has_z else None
+        A = -(1.0 + 15.0 * torch.rand(h, generator=gen))  # Mamba-2 A = -exp(U(log 1, log 16)) range
+        if regime == "wide":
+            dt = torch.randn(b, l, h, generator=gen) * 0.5
+            dt_bias = torch.rand(h, generator=gen) * 0.1 if has_bias else None
+        else:  # Mamba-2 initialisation: softplus(dt_bias) in [1e-3, 1e-1], long memory
+            dt = torch.randn(b, l, h, generator=gen) * 0.1
+            tgt = torch.exp(torch.rand(h, generator=gen) * (math.log(0.1) - math.log(1e-3)) + math.log(1e-3))
+            dt_bias = tgt + torch.log(-torch.expm1(-tgt)) if has_bias else None
+            if not has_bias:
+                dt = dt - 4.0
+        D = None if dmode is None else (torch.randn(h, generator=gen) if dmode == "h" else
+                                        torch.randn(h, p, generator=gen))
+        u1 = x.permute(0, 2, 3, 1).reshape(b, h * p, l)
+        d1 = dt.permute(0, 2, 1)[:, :, None, :].expand(b, h, p, l).reshape(b, h * p, l)
+        A1 = A[:, None, None].expand(h, p, n).reshape(h * p, n)
+        B1, C1 = B.permute(0, 2, 3, 1).contiguous(), C.permute(0, 2, 3, 1).contiguous()
+        D1 = None if D is None else (D[:, None].expand(h, p) if D.dim() == 1 else D).reshape(h * p)
+        z1 = None if z is None else z.permute(0, 2, 3, 1).reshape(b, h * p, l)
+        b1 = None if dt_bias is None else dt_bias[:, None].expand(h, p).reshape(h * p)
+        with torch.no_grad():
+            out1, last1 = m.selective_scan_fn(u1.contiguous(), d1.contiguous(), A1.contiguous(), B1, C1,
+                                              None if D1 is None else D1.contiguous(),
+                                              None if z1 is None else z1.contiguous(),
+                                              None if b1 is None else b1.contiguous(),
+                                              delta_softplus=True, return_last_state=True)
+        out = out1.reshape(b, h, p, l).permute(0, 3, 1, 2)
+        final = last1.reshape(b, h, p, n)
+        st.add("ssd", dict(dt_softplus=True, D=dmode, regime=regime), dict(
+            in_x=_np(x), in_dt=_np(dt), in_A=_np(A), in_B=_np(B), in_C=_np(C), in_D=_np(D), in_z=_np(z),
+            in_dt_bias=_np(dt_bias), out=_np(out), final_states=_np(final)))
+    st.save("ssd.npz")
+
+
 if __name__ == "__main__":
     mod = _import_reference()
     print("reference:", mod.__file__, "isa:", sys.modules["mamba_cpu._C"].cpu_isa())
     make_scan(mod)
     make_conv(mod)
     make_state_update(mod)
+    make_ssd(mod)

@@ -43,6 +43,7 @@ _STRUCTS = {
     "mb200_conv1d_params": _lib.Conv1dParams,
     "mb200_state_update_params": _lib.StateUpdateParams,
     "mb200_conv1d_update_params": _lib.Conv1dUpdateParams,
+    "mb200_ssd_params": _lib.SsdParams,
 }
 
 

@@ -117,3 +117,13 @@ def test_oracle_is_deterministic_across_thread_counts():
     for k in a:
         if a[k] is not None:
             assert np.array_equal(a[k], b[k]), k
+
+
+@pytest.mark.parametrize("meta,a", _cases("ssd", "ssd"))
+def test_ssd_oracle_matches_reference(meta, a):
+    """The float64 SSD recurrence against the reference's own kernel run on the equivalent Mamba-1
+    problem (channels = nheads * headdim; tests/golden/make_golden.py:make_ssd)."""
+    out, fin = f64.ssd_fwd(a["in_x"], a["in_dt"], a["in_A"], a["in_B"], a["in_C"], a.get("in_D"), a.get("in_z"),
+                           a.get("in_dt_bias"), dt_softplus=meta["dt_softplus"])
+    assert_close(out, a["out"], 1e-4, 1e-5, "out", norm_tol=1e-5)
+    assert_close(fin, a["final_states"], 1e-4, 1e-5, "final_states", norm_tol=1e-5)
