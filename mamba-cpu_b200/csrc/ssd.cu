@@ -19,15 +19,25 @@
 // both bf16), so the carried state enters the product with ~16 significant bits; M and X' are
 // rounded to bf16 once.
 //
-// Shared memory (PT = 32 headdim columns per CTA, 98 KB, two CTAs per SM):
-//   sCM  [128 t][128 n]  C tile, then (once C B^T and C S^T are done) M [128 i][128 j]
-//   sB   [128 t][128 n]  B tile; K-major operand of C B^T, MN-major operand of X'^T B
-//   sX   [128 t][PT]     X tile (MN-major operand of M X)
-//   sXs  [128 t][PT]     X' (MN-major operand of X'^T B)
-//   sSh, sSl [128 n][PT] bf16 hi / lo parts of S (MN-major operand of C S^T)
+// Shared memory (PT = 32 headdim columns per CTA, 98 KB, two CTAs per SM). Every tile is stored
+// as [column piece c8][row r][8 elements]: 16 bytes per (row, 8 columns), so core matrix
+// (r / 8, c8) -- 8 rows x 16 bytes -- is 128 contiguous bytes, the rows of one column piece are
+// contiguous, and the same bytes serve as a K-major operand (rows = M / N) or an MN-major one
+// (rows = K). A 5-D TMA tensor map per input (8 elements, seqlen, column pieces, group / head,
+// batch) writes exactly this order, so one bulk tensor copy loads a tile; rows past seqlen are
+// zero-filled by the copy.
+//   sCM  [16][128 t]     C tile, then (once C B^T and C S^T are done) M [128 i][128 j]
+//   sB   [16][128 t]     B tile; K-major operand of C B^T, MN-major operand of X'^T B
+//   sX   [PT/8][128 t]   X tile (MN-major operand of M X)
+//   sXs  [PT/8][128 t]   X' (MN-major operand of X'^T B)
+//   sSh, sSl [PT/8][128 n]  bf16 hi / lo parts of S (MN-major operand of C S^T)
 // dstate is zero-padded to 128 (the padded columns of B stay zero, so S's padded rows stay zero).
 // TMEM (256 columns): [0, 128) G, then M X; [128, 128 + PT) C S^T; [128 + PT, 128 + 2 PT) X'^T B.
-// Thread i of the 128 reads row i of every accumulator (TMEM lane i).
+// The chunk's tiles are copied in while the previous chunk's outputs are written: the copies for
+// chunk k + 1 are issued as soon as chunk k's last products have completed.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include "common.cuh"
 #include "stage.cuh"
 #include "tmem.cuh"
@@ -39,7 +49,7 @@ namespace {
 constexpr int kQ = 128;        // steps per chunk (the M of every product)
 constexpr int kNP = 128;       // dstate padded
 constexpr int kPT = 32;        // headdim columns per CTA
-constexpr int kSsdThreads = 128;
+constexpr int kSsdThreads = 256;
 constexpr uint32_t kSsdTmemCols = 256;
 
 constexpr int kTileCM = kQ * kNP * 2;   // bytes
@@ -54,7 +64,7 @@ constexpr int kOffSl = kOffSh + kTileS;
 constexpr int kOffF = kOffSl + kTileS;             // float area
 constexpr int kFloats = 2 * kQ + 8 + kPT;          // dt, cs, warp sums, D
 constexpr int kOffBar = kOffF + kFloats * 4;
-constexpr int kSsdSmem = kOffBar + 16;
+constexpr int kSsdSmem = kOffBar + 32;
 
 struct SsdArgs {
   const __nv_bfloat16* x;
@@ -75,11 +85,8 @@ struct SsdArgs {
   int ntiles;  // P / kPT
 };
 
-// Byte offset of the 16-byte piece (row r, column chunk c8 = column / 8) of a core-matrix tiled
-// bf16 tile with `cols` columns: core matrix (r / 8, c8) holds rows r..r+7 x 8 columns, 128 bytes.
-__device__ __forceinline__ uint32_t core16(int r, int c8, int cols) {
-  return (uint32_t)(((r >> 3) * (cols >> 3) + c8) * 128 + (r & 7) * 16);
-}
+// Byte offset of the 16-byte piece (row r, column piece c8 = column / 8) of a 128-row tile.
+__device__ __forceinline__ uint32_t core16(int r, int c8) { return (uint32_t)((c8 * kQ + r) * 16); }
 
 // Shared-memory matrix descriptor, no swizzle (sm_100 version 1): start address, leading byte
 // offset (between core matrices adjacent along K) and stride byte offset (between core matrices
@@ -110,11 +117,6 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
                : "memory");
 }
 
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
-}
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
-
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<const uint32_t*>(&v);
@@ -123,22 +125,60 @@ __device__ __forceinline__ float2 unpack_bf16(uint32_t w) {
   return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w));
 }
 
-// A [rows][cols] bf16 tile piece by piece from global rows (row r at base + r * row_stride
-// elements, 16-byte aligned), rows >= valid_rows zero-filled.
-__device__ __forceinline__ void load_tile(uint32_t s_tile, const __nv_bfloat16* base, int64_t row_stride,
-                                          int rows, int cols_loaded, int cols, int valid_rows, int tid) {
-  const int nc8 = cols_loaded >> 3;
-  for (int i = tid; i < rows * nc8; i += kSsdThreads) {
-    const int r = i / nc8, c8 = i - r * nc8;
-    const bool ok = r < valid_rows;
-    const __nv_bfloat16* src = base + (ok ? (int64_t)r * row_stride : 0) + c8 * 8;
-    cp_async16(s_tile + core16(r, c8, cols), src, ok ? 16u : 0u);
+// Wait for the mbarrier phase with the given parity (tensor-core completion): a tight try_wait
+// loop, bounded by 2 s of GPU time (%globaltimer); on timeout the fault word records it and the
+// kernel carries on.
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void mbar_wait_spin(uint64_t* bar, uint32_t parity) {
+  const uint32_t addr = smem_u32(bar);
+  uint64_t t_start = 0;
+  for (uint32_t i = 0;; ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    if (done) return;
+    if ((i & 1023u) == 0) {
+      const uint64_t t = global_ns();
+      if (i == 0)
+        t_start = t;
+      else if (t - t_start > 2000000000ull)
+        break;
+    }
   }
+  atomicOr(&g_mb200_fault, kFaultWaitTimeout);
 }
 
-__global__ void __launch_bounds__(kSsdThreads, 2) ssd_fwd_kernel(SsdArgs a) {
+// One 5-D bulk tensor copy (TMA, no multicast) of the box at coordinates c0..c4 into shared memory,
+// completing on `bar` (transaction bytes).
+__device__ __forceinline__ void tma_load_5d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
+                                            int c4, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5, "
+      "%6}], [%7];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4), "r"(smem_u32(bar))
+      : "memory");
+}
+
+struct SsdMaps {
+  CUtensorMap B, C, x;
+};
+
+// Thread roles (256 threads): row = tid % 128 is the thread's accumulator row (TMEM lane; warps w
+// and w + 4 share lanes 32 (w % 4) .. + 31) and half = tid / 128 picks its half of the columns:
+// headdim columns [16 half, 16 half + 16) of the outputs and of S, and the 16-wide column pieces
+// q with q % 2 == half of M (so both halves of a row get the same number of non-zero pieces).
+__global__ void __launch_bounds__(kSsdThreads, 2) ssd_fwd_kernel(SsdArgs a, const __grid_constant__ SsdMaps maps) {
   extern __shared__ __align__(1024) uint8_t smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int row = tid & (kQ - 1), half = tid >> 7, rw = warp & 3;
+  constexpr int kPH = kPT / 2;  // headdim columns per half
   const int tile = blockIdx.x % a.ntiles;
   const int64_t bh = blockIdx.x / a.ntiles;
   const int64_t h = bh % a.H, b = bh / a.H;
@@ -149,93 +189,103 @@ __global__ void __launch_bounds__(kSsdThreads, 2) ssd_fwd_kernel(SsdArgs a) {
   float* scs = sdt + kQ;
   float* swarp = scs + kQ;
   float* sD = swarp + 8;
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kOffBar);
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + kOffBar + 8);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kOffBar);       // tensor-core completion
+  uint64_t* tbar = reinterpret_cast<uint64_t*>(smem + kOffBar + 8);  // tile copies
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + kOffBar + 16);
   const uint32_t s0 = smem_u32(smem);
   const uint32_t sCM = s0, sB = s0 + kOffB, sX = s0 + kOffX, sXs = s0 + kOffXs, sSh = s0 + kOffSh,
                  sSl = s0 + kOffSl;
-
-  if (warp == 0) tmem_alloc(tslot, kSsdTmemCols);
-  if (tid == 0) {
-    mbar_init(bar, 1);
-    mbar_fence_init();
-  }
   const int N = (int)a.N;
   const int nc8 = N / 8;                       // 16-byte pieces of a B / C row
   const int ksteps = (N + 15) / 16;            // K steps of the dstate contractions
-  // zero the padded dstate columns of B (kept zero) and, if dstate is an odd multiple of 8, the
-  // piece of C the last K step reads past dstate (re-zeroed every chunk, as M overwrites it)
-  for (int i = tid; i < kQ * (16 - nc8); i += kSsdThreads) {
-    const int r = i / (16 - nc8), c8 = nc8 + i % (16 - nc8);
-    *reinterpret_cast<uint4*>(smem + kOffB + core16(r, c8, kNP)) = make_uint4(0, 0, 0, 0);
+  const int64_t nchunks = (a.L + kQ - 1) / kQ;
+  const uint32_t tile_bytes = (uint32_t)(2 * kQ * 16 * nc8 + kTileX);
+
+  if (warp == 0) tmem_alloc(tslot, kSsdTmemCols);
+  // zero the padded dstate columns of B (the copies never write them)
+  for (int i = tid; i < kQ * 16; i += kSsdThreads) {
+    const int r = i & (kQ - 1), c8 = i >> 7;
+    if (c8 >= nc8) *reinterpret_cast<uint4*>(smem + kOffB + core16(r, c8)) = make_uint4(0, 0, 0, 0);
+  }
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    mbar_init(tbar, 1);
+    mbar_fence_init();
+    if (nchunks > 0) {
+      mbar_arrive_expect_tx(tbar, tile_bytes);
+      tma_load_5d(sCM, &maps.C, 0, 0, 0, (int)g, (int)b, tbar);
+      tma_load_5d(sB, &maps.B, 0, 0, 0, (int)g, (int)b, tbar);
+      tma_load_5d(sX, &maps.x, 0, 0, p0 / 8, (int)h, (int)b, tbar);
+    }
   }
   if (tid < kPT) {
     float dv = 0.f;
     if (a.D != nullptr) dv = a.D_per_dim ? a.D[h * a.P + p0 + tid] : a.D[h];
     sD[tid] = dv;
   }
-  // S row n = tid (float32), initial state or zeros
-  float S[kPT];
-  {
-    const int n = tid;
+  // S row n = row, columns [kPH half, + kPH) (float32): initial state or zeros
+  float S[kPH];
 #pragma unroll
-    for (int p = 0; p < kPT; ++p)
-      S[p] = (a.init != nullptr && n < N) ? a.init[((b * a.H + h) * a.P + p0 + p) * a.N + n] : 0.f;
-  }
+  for (int p = 0; p < kPH; ++p)
+    S[p] = (a.init != nullptr && row < N) ? a.init[((b * a.H + h) * a.P + p0 + kPH * half + p) * a.N + row] : 0.f;
   const float A2 = a.A[h] * kLog2e;
   const float bias = a.dt_bias != nullptr ? a.dt_bias[h] : 0.f;
+  const __nv_bfloat16* zbase = a.z != nullptr ? a.z + b * a.zbs + h * a.zhs + p0 + kPH * half : nullptr;
+  const float* dtbase = a.dt + b * a.dtbs + h;
 
   tmem_fence_before_sync();
   __syncthreads();
   tmem_fence_after_sync();
   const uint32_t tbase = *tslot;
-  const uint32_t trow = tbase + ((uint32_t)(warp * 32) << 16);  // this warp's lanes
+  const uint32_t trow = tbase + ((uint32_t)(rw * 32) << 16);  // this warp's lanes
 
   constexpr uint32_t kIdG = idesc_bf16(kQ, kQ, 0, 0);
   constexpr uint32_t kIdY = idesc_bf16(kQ, kPT, 0, 1);
   constexpr uint32_t kIdS = idesc_bf16(kNP, kPT, 1, 1);
-  constexpr uint32_t kLboK = 128, kSboK = (kNP / 8) * 128;      // K-major 128-column tiles
-  constexpr uint32_t kLboP = (kPT / 8) * 128, kSboP = 128;      // MN-major PT-column tiles
+  // Column-piece-major tiles: core matrices 128 bytes apart along the rows, kQ * 16 bytes apart
+  // along the column pieces. K-major (rows = M / N): LBO = piece stride, SBO = 128; MN-major
+  // (rows = K): LBO = 128, SBO = piece stride. A K step of 16 is two pieces (K-major) or two
+  // 8-row groups (MN-major).
+  constexpr uint32_t kPiece = kQ * 16;
   constexpr uint32_t kColYo = kQ, kColSl = kQ + kPT;
 
-  uint32_t phase = 0;
-  const int64_t nchunks = (a.L + kQ - 1) / kQ;
+  uint32_t phase = 0, tphase = 0;
+  float dt_raw = (half == 0 && row < a.L) ? dtbase[row * a.dtls] : 0.f;
   for (int64_t k = 0; k < nchunks; ++k) {
     const int64_t t0 = k * kQ;
     const int valid = (int)(a.L - t0 < kQ ? a.L - t0 : kQ);
 
-    // ---- S_prev as bf16 hi + lo (row n = tid), the chunk's tiles, dt and its cumulative sum
-    {
-      const int n = tid;
+    // ---- S_prev as bf16 hi + lo, this chunk's z (registers), dt and its cumulative sum
+    uint4 zv[kPH / 8];
+    if (zbase != nullptr && row < valid) {
 #pragma unroll
-      for (int c8 = 0; c8 < kPT / 8; ++c8) {
-        uint32_t hi[4], lo[4];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const float v0 = S[c8 * 8 + 2 * q], v1 = S[c8 * 8 + 2 * q + 1];
-          hi[q] = pack_bf16(v0, v1);
-          const float2 hv = unpack_bf16(hi[q]);
-          lo[q] = pack_bf16(v0 - hv.x, v1 - hv.y);
-        }
-        *reinterpret_cast<uint4*>(smem + kOffSh + core16(n, c8, kPT)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-        *reinterpret_cast<uint4*>(smem + kOffSl + core16(n, c8, kPT)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-      }
+      for (int c = 0; c < kPH / 8; ++c) zv[c] = __ldg(reinterpret_cast<const uint4*>(zbase + (t0 + row) * a.zls) + c);
     }
-    load_tile(sCM, a.C + b * a.Cbs + t0 * a.Cls + g * a.Cgs, a.Cls, kQ, N, kNP, valid, tid);
-    load_tile(sB, a.B + b * a.Bbs + t0 * a.Bls + g * a.Bgs, a.Bls, kQ, N, kNP, valid, tid);
-    load_tile(sX, a.x + b * a.xbs + t0 * a.xls + h * a.xhs + p0, a.xls, kQ, kPT, kPT, valid, tid);
-    asm volatile("cp.async.commit_group;" ::: "memory");
-    if (nc8 & 1)  // C columns [dstate, dstate + 8) of the last K step
-      *reinterpret_cast<uint4*>(smem + core16(tid, nc8, kNP)) = make_uint4(0, 0, 0, 0);
-    float cs;
-    {
+#pragma unroll
+    for (int c = 0; c < kPH / 8; ++c) {
+      uint32_t hi[4], lo[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float v0 = S[c * 8 + 2 * q], v1 = S[c * 8 + 2 * q + 1];
+        hi[q] = pack_bf16(v0, v1);
+        const float2 hv = unpack_bf16(hi[q]);
+        lo[q] = pack_bf16(v0 - hv.x, v1 - hv.y);
+      }
+      const uint32_t off = core16(row, (kPH / 8) * half + c);
+      *reinterpret_cast<uint4*>(smem + kOffSh + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+      *reinterpret_cast<uint4*>(smem + kOffSl + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    }
+    if ((nc8 & 1) && half == 1)  // C columns [dstate, dstate + 8) of the last K step (M overwrote them)
+      *reinterpret_cast<uint4*>(smem + core16(row, nc8)) = make_uint4(0, 0, 0, 0);
+    float cs = 0.f;
+    if (half == 0) {
       float dtv = 0.f;
-      if (tid < valid) {
-        float raw = a.dt[b * a.dtbs + (t0 + tid) * a.dtls + h] + bias;
+      if (row < valid) {
+        float raw = dt_raw + bias;
         if (a.softplus) raw = softplus_f(raw);
         dtv = fminf(fmaxf(raw, a.dt_min), a.dt_max);
       }
-      sdt[tid] = dtv;
+      sdt[row] = dtv;
       float v = dtv * A2;  // log2 units
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
@@ -243,149 +293,188 @@ __global__ void __launch_bounds__(kSsdThreads, 2) ssd_fwd_kernel(SsdArgs a) {
         if (lane >= o) v += u;
       }
       if (lane == 31) swarp[warp] = v;
-      __syncthreads();
-      for (int w = 0; w < warp; ++w) v += swarp[w];
       cs = v;
-      scs[tid] = v;
+      // the next chunk's dt (its latency overlaps this chunk)
+      dt_raw = (t0 + kQ + row < a.L) ? dtbase[(t0 + kQ + row) * a.dtls] : 0.f;
     }
-    cp_async_wait_all();
+    __syncthreads();
+    if (half == 0) {
+      for (int w = 0; w < rw; ++w) cs += swarp[w];
+      scs[row] = cs;
+    }
+    mbar_wait_spin(tbar, tphase);  // this chunk's tiles have landed
+    tphase ^= 1;
     fence_proxy_async();
     tmem_fence_before_sync();
     __syncthreads();
     const float cs_end = scs[kQ - 1];
+    cs = scs[row];
 
     // ---- G = C B^T and Yo = C S^T (hi, then lo)
     if (tid == 0) {
       tmem_fence_after_sync();
       for (int s = 0; s < ksteps; ++s)
-        umma_bf16(tbase, sdesc(sCM + s * 256, kLboK, kSboK), sdesc(sB + s * 256, kLboK, kSboK), kIdG, s > 0);
-      for (int s = 0; s < ksteps; ++s)
-        umma_bf16(tbase + kColYo, sdesc(sCM + s * 256, kLboK, kSboK), sdesc(sSh + s * 2 * kLboP, kLboP, kSboP), kIdY,
+        umma_bf16(tbase, sdesc(sCM + s * 2 * kPiece, kPiece, 128), sdesc(sB + s * 2 * kPiece, kPiece, 128), kIdG,
                   s > 0);
       for (int s = 0; s < ksteps; ++s)
-        umma_bf16(tbase + kColYo, sdesc(sCM + s * 256, kLboK, kSboK), sdesc(sSl + s * 2 * kLboP, kLboP, kSboP), kIdY,
+        umma_bf16(tbase + kColYo, sdesc(sCM + s * 2 * kPiece, kPiece, 128), sdesc(sSh + s * 256, 128, kPiece), kIdY,
+                  s > 0);
+      for (int s = 0; s < ksteps; ++s)
+        umma_bf16(tbase + kColYo, sdesc(sCM + s * 2 * kPiece, kPiece, 128), sdesc(sSl + s * 256, 128, kPiece), kIdY,
                   1);
       umma_commit(bar);
     }
-    mbar_wait(bar, phase);
+    mbar_wait_spin(bar, phase);
     phase ^= 1;
     tmem_fence_after_sync();
 
-    // ---- M = G o L (row i = tid) over C's tile, and X' = w X
+    // ---- M = G o L over C's tile (row i, pieces q % 2 == half), X' = w X (this half's columns)
+    uint4 xv[kPH / 8];  // this row's x, kept for the output stage (the next chunk's copy reuses sX)
     {
-      const int i = tid;
+      const int i = row;
+      const int nz = 2 * rw + 2;  // pieces of this warp's rows that reach the diagonal
 #pragma unroll 1
-      for (int q = 0; q < kQ / 16; ++q) {
+      for (int q = half; q < kQ / 16; q += 2) {
         uint4 w0 = make_uint4(0, 0, 0, 0), w1 = make_uint4(0, 0, 0, 0);
-        if (q <= 2 * warp + 1) {  // warp-uniform: some row of this warp reaches column 16 q
+        if (q < nz) {  // warp-uniform
           float gv[16];
           tmem_ld16(trow + q * 16, gv);
           tmem_wait_ld();
           uint32_t pk[8];
 #pragma unroll
-          for (int jj = 0; jj < 16; jj += 2) {
+          for (int jj = 0; jj < 16; jj += 4) {
             const int j = q * 16 + jj;
-            const float4 cj = *reinterpret_cast<const float4*>(&scs[j & ~3]);
-            const float c0 = (jj & 2) ? cj.z : cj.x, c1 = (jj & 2) ? cj.w : cj.y;
-            const float m0 = j <= i ? gv[jj] * ex2(cs - c0) * sdt[j] : 0.f;
-            const float m1 = j + 1 <= i ? gv[jj + 1] * ex2(cs - c1) * sdt[j + 1] : 0.f;
+            const float4 cj = *reinterpret_cast<const float4*>(&scs[j]);
+            const float4 dj = *reinterpret_cast<const float4*>(&sdt[j]);
+            const float m0 = j <= i ? gv[jj] * ex2(cs - cj.x) * dj.x : 0.f;
+            const float m1 = j + 1 <= i ? gv[jj + 1] * ex2(cs - cj.y) * dj.y : 0.f;
+            const float m2 = j + 2 <= i ? gv[jj + 2] * ex2(cs - cj.z) * dj.z : 0.f;
+            const float m3 = j + 3 <= i ? gv[jj + 3] * ex2(cs - cj.w) * dj.w : 0.f;
             pk[jj / 2] = pack_bf16(m0, m1);
+            pk[jj / 2 + 1] = pack_bf16(m2, m3);
           }
           w0 = make_uint4(pk[0], pk[1], pk[2], pk[3]);
           w1 = make_uint4(pk[4], pk[5], pk[6], pk[7]);
         }
-        *reinterpret_cast<uint4*>(smem + core16(i, 2 * q, kQ)) = w0;
-        *reinterpret_cast<uint4*>(smem + core16(i, 2 * q + 1, kQ)) = w1;
+        *reinterpret_cast<uint4*>(smem + core16(i, 2 * q)) = w0;
+        *reinterpret_cast<uint4*>(smem + core16(i, 2 * q + 1)) = w1;
       }
       const float wx = ex2(cs_end - cs) * sdt[i];
 #pragma unroll
-      for (int c8 = 0; c8 < kPT / 8; ++c8) {
-        const uint4 v = *reinterpret_cast<const uint4*>(smem + kOffX + core16(i, c8, kPT));
-        const uint32_t in[4] = {v.x, v.y, v.z, v.w};
+      for (int c = 0; c < kPH / 8; ++c) {
+        const uint32_t off = core16(i, (kPH / 8) * half + c);
+        xv[c] = *reinterpret_cast<const uint4*>(smem + kOffX + off);
+        const uint32_t in[4] = {xv[c].x, xv[c].y, xv[c].z, xv[c].w};
         uint32_t o[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const float2 f = unpack_bf16(in[e]);
           o[e] = pack_bf16(f.x * wx, f.y * wx);
         }
-        *reinterpret_cast<uint4*>(smem + kOffXs + core16(i, c8, kPT)) = make_uint4(o[0], o[1], o[2], o[3]);
+        *reinterpret_cast<uint4*>(smem + kOffXs + off) = make_uint4(o[0], o[1], o[2], o[3]);
       }
     }
     fence_proxy_async();
     tmem_fence_before_sync();
     __syncthreads();
 
-    // ---- Yd = M X (into G's columns) and Sl = X'^T B
+    // ---- Yd = M X (into G's columns) and Sl = X'^T B; then the next chunk's tile copies
     if (tid == 0) {
       tmem_fence_after_sync();
       for (int s = 0; s < kQ / 16; ++s)
-        umma_bf16(tbase, sdesc(sCM + s * 256, kLboK, kSboK), sdesc(sX + s * 2 * kLboP, kLboP, kSboP), kIdY, s > 0);
+        umma_bf16(tbase, sdesc(sCM + s * 2 * kPiece, kPiece, 128), sdesc(sX + s * 256, 128, kPiece), kIdY, s > 0);
       for (int s = 0; s < kQ / 16; ++s)
-        umma_bf16(tbase + kColSl, sdesc(sB + s * 2 * kSboK, kSboK, 128), sdesc(sXs + s * 2 * kLboP, kLboP, kSboP),
-                  kIdS, s > 0);
+        umma_bf16(tbase + kColSl, sdesc(sB + s * 256, 128, kPiece), sdesc(sXs + s * 256, 128, kPiece), kIdS, s > 0);
       umma_commit(bar);
     }
-    mbar_wait(bar, phase);
+    mbar_wait_spin(bar, phase);
     phase ^= 1;
     tmem_fence_after_sync();
+    if (tid == 0 && k + 1 < nchunks) {
+      const int tn = (int)(t0 + kQ);
+      mbar_arrive_expect_tx(tbar, tile_bytes);
+      tma_load_5d(sCM, &maps.C, 0, tn, 0, (int)g, (int)b, tbar);
+      tma_load_5d(sB, &maps.B, 0, tn, 0, (int)g, (int)b, tbar);
+      tma_load_5d(sX, &maps.x, 0, tn, p0 / 8, (int)h, (int)b, tbar);
+    }
 
-    // ---- outputs of row i = tid, and the carried state (row n = tid)
+    // ---- outputs of row i, columns [kPH half, + kPH), and the carried state (row n = row)
     {
-      float yo[kPT], yd[kPT], sl[kPT];
-      tmem_ld16(trow + kColYo, *reinterpret_cast<float(*)[16]>(&yo[0]));
-      tmem_ld16(trow + kColYo + 16, *reinterpret_cast<float(*)[16]>(&yo[16]));
-      tmem_ld16(trow, *reinterpret_cast<float(*)[16]>(&yd[0]));
-      tmem_ld16(trow + 16, *reinterpret_cast<float(*)[16]>(&yd[16]));
-      tmem_ld16(trow + kColSl, *reinterpret_cast<float(*)[16]>(&sl[0]));
-      tmem_ld16(trow + kColSl + 16, *reinterpret_cast<float(*)[16]>(&sl[16]));
+      float yo[kPH], yd[kPH], sl[kPH];
+      const uint32_t cb = kPH * half;
+      tmem_ld16(trow + kColYo + cb, yo);
+      tmem_ld16(trow + cb, yd);
+      tmem_ld16(trow + kColSl + cb, sl);
       tmem_wait_ld();
-      const int i = tid;
+      const int i = row;
       if (i < valid) {
         const float eo = ex2(cs);
         const int64_t t = t0 + i;
-        __nv_bfloat16* orow = a.out + ((b * a.L + t) * a.H + h) * a.P + p0;
-        const __nv_bfloat16* zrow = a.z != nullptr ? a.z + b * a.zbs + t * a.zls + h * a.zhs + p0 : nullptr;
+        __nv_bfloat16* orow = a.out + ((b * a.L + t) * a.H + h) * a.P + p0 + cb;
 #pragma unroll
-        for (int c8 = 0; c8 < kPT / 8; ++c8) {
-          const uint4 xv = *reinterpret_cast<const uint4*>(smem + kOffX + core16(i, c8, kPT));
-          const uint32_t xin[4] = {xv.x, xv.y, xv.z, xv.w};
-          uint32_t zin[4] = {0, 0, 0, 0};
-          if (zrow != nullptr) {
-            const uint4 zv = __ldg(reinterpret_cast<const uint4*>(zrow + c8 * 8));
-            zin[0] = zv.x, zin[1] = zv.y, zin[2] = zv.z, zin[3] = zv.w;
-          }
+        for (int c = 0; c < kPH / 8; ++c) {
+          const uint32_t xin[4] = {xv[c].x, xv[c].y, xv[c].z, xv[c].w};
+          const uint32_t zin[4] = {zv[c].x, zv[c].y, zv[c].z, zv[c].w};
           uint32_t o[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const int p = c8 * 8 + 2 * e;
+            const int p = c * 8 + 2 * e;
             const float2 xf = unpack_bf16(xin[e]);
-            float y0 = fmaf(eo, yo[p], yd[p]) + sD[p] * xf.x;
-            float y1 = fmaf(eo, yo[p + 1], yd[p + 1]) + sD[p + 1] * xf.y;
-            if (zrow != nullptr) {
+            float y0 = fmaf(eo, yo[p], yd[p]) + sD[cb + p] * xf.x;
+            float y1 = fmaf(eo, yo[p + 1], yd[p + 1]) + sD[cb + p + 1] * xf.y;
+            if (zbase != nullptr) {
               const float2 zf = unpack_bf16(zin[e]);
               y0 *= silu_f(zf.x);
               y1 *= silu_f(zf.y);
             }
             o[e] = pack_bf16(y0, y1);
           }
-          *reinterpret_cast<uint4*>(orow + c8 * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+          *reinterpret_cast<uint4*>(orow + c * 8) = make_uint4(o[0], o[1], o[2], o[3]);
         }
       }
       const float decay = ex2(cs_end);
 #pragma unroll
-      for (int p = 0; p < kPT; ++p) S[p] = fmaf(decay, S[p], sl[p]);
+      for (int p = 0; p < kPH; ++p) S[p] = fmaf(decay, S[p], sl[p]);
     }
     tmem_fence_before_sync();
     __syncthreads();
   }
 
-  if (a.final_states != nullptr && tid < N) {
+  if (a.final_states != nullptr && row < N) {
 #pragma unroll
-    for (int p = 0; p < kPT; ++p) a.final_states[((b * a.H + h) * a.P + p0 + p) * a.N + tid] = S[p];
+    for (int p = 0; p < kPH; ++p) a.final_states[((b * a.H + h) * a.P + p0 + kPH * half + p) * a.N + row] = S[p];
   }
   tmem_fence_before_sync();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tbase, kSsdTmemCols);
+}
+
+// cuTensorMapEncodeTiled from the driver (through the runtime, no libcuda link).
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (fn == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// Tensor map of a bf16 tensor seen as (8 elements, seqlen, pieces of 8 columns, group or head,
+// batch) with element strides (1, s_l, 8, s_g, s_b); box (8, 128, box_pieces, 1, 1).
+bool encode_map(CUtensorMap* m, const void* base, int64_t L, int64_t pieces, int64_t ng, int64_t nb, int64_t s_l,
+                int64_t s_g, int64_t s_b, int box_pieces) {
+  PFN_cuTensorMapEncodeTiled_v12000 fn = encode_fn();
+  if (fn == nullptr) return false;
+  const cuuint64_t dims[5] = {8, (cuuint64_t)L, (cuuint64_t)pieces, (cuuint64_t)ng, (cuuint64_t)nb};
+  const cuuint64_t strides[4] = {(cuuint64_t)s_l * 2, 16, (cuuint64_t)s_g * 2, (cuuint64_t)s_b * 2};
+  const cuuint32_t box[5] = {8, (cuuint32_t)kQ, (cuuint32_t)box_pieces, 1, 1};
+  const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 }  // namespace
@@ -408,7 +497,7 @@ MB200_API int mb200_ssd_chunk_scan_fwd(const mb200_ssd_params* p, void* stream) 
   if (p->nheads % p->ngroups != 0) return MB200_ERR_BAD_SHAPE;
   if (p->x_dtype != MB200_BF16) return p->x_dtype == MB200_F32 || p->x_dtype == MB200_F16 ? MB200_ERR_UNSUPPORTED
                                                                                           : MB200_ERR_BAD_DTYPE;
-  if (p->dstate % 8 != 0 || p->dstate > kNP || p->headdim % kPT != 0 || p->headdim > 256)
+  if (p->dstate % 8 != 0 || p->dstate > kNP || p->headdim % kPT != 0 || p->headdim > 256 || p->seqlen > 0x7fffffff)
     return MB200_ERR_UNSUPPORTED;
   // 16-byte pieces: row starts of x, z, B, C and out aligned
   const bool al = aligned16(p->x) && aligned16(p->B) && aligned16(p->C) && aligned16(p->out) &&
@@ -446,9 +535,18 @@ MB200_API int mb200_ssd_chunk_scan_fwd(const mb200_ssd_params* p, void* stream) 
   a.softplus = p->dt_softplus != 0;
   a.D_per_dim = p->D_per_dim != 0;
   a.ntiles = (int)ntiles;
+  SsdMaps maps;
+  const int64_t L = p->seqlen > 0 ? p->seqlen : 1;
+  if (!encode_map(&maps.B, p->B, L, p->dstate / 8, p->ngroups, p->batch, p->B_seqlen_stride, p->B_group_stride,
+                  p->B_batch_stride, (int)(p->dstate / 8)) ||
+      !encode_map(&maps.C, p->C, L, p->dstate / 8, p->ngroups, p->batch, p->C_seqlen_stride, p->C_group_stride,
+                  p->C_batch_stride, (int)(p->dstate / 8)) ||
+      !encode_map(&maps.x, p->x, L, p->headdim / 8, p->nheads, p->batch, p->x_seqlen_stride, p->x_head_stride,
+                  p->x_batch_stride, kPT / 8))
+    return MB200_ERR_CUDA;
   cudaError_t e = cudaFuncSetAttribute(ssd_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSsdSmem);
   if (e != cudaSuccess) return MB200_ERR_CUDA;
-  ssd_fwd_kernel<<<(unsigned)ctas, kSsdThreads, kSsdSmem, static_cast<cudaStream_t>(stream)>>>(a);
+  ssd_fwd_kernel<<<(unsigned)ctas, kSsdThreads, kSsdSmem, static_cast<cudaStream_t>(stream)>>>(a, maps);
   if (cudaGetLastError() != cudaSuccess) return MB200_ERR_CUDA;
   note_launches(1);
   return MB200_OK;
