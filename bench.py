@@ -27,7 +27,9 @@ At N = 1 the line also carries a "c2" block: BASELINE config 2 (fp32, batch 4, d
 1024, z, delta_bias), the north-star's fp32 configuration, with its own roofline and CPU baseline;
 and "c3" / "c4" blocks: BASELINE configs 3 and 4 at model level (transformers' MambaForCausalLM,
 random init, routed to this package by hf.patch_transformers): the 130M prefill in fp32 and the
-1.4B-shape training step in bf16, in tokens/s, device-timed and end to end.
+1.4B-shape training step in bf16, in tokens/s, device-timed and end to end; and an "ssd" block: the
+Mamba-2 SSD chunk scan forward (mamba_chunk_scan_combined) at the Mamba-2 2.7B layer shape, with its
+roofline and the reference's CPU kernel on the equivalent Mamba-1 problem as its CPU baseline.
 
 `--impl reference` times the reference's own CPU kernel (mamba-cpu csrc/selective_scan.cpp built
 into oracle/_ref) with the reference's Python-side steps (B/C transpose to (b, g, l, n), zeroed
@@ -689,6 +691,126 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+SSD = dict(batch=2, seqlen=4096, nheads=80, headdim=64, ngroups=1, dstate=128,
+           desc="Mamba-2 SSD chunk scan forward (mamba_chunk_scan_combined, a roadmap item of the reference) at the "
+                "Mamba-2 2.7B layer shape: b=2, seqlen 4096, 80 heads x headdim 64 (d_inner 5120), dstate 128, "
+                "ngroups 1; bf16 x/z/B/C, fp32 dt/A/D/dt_bias, softplus, z gate")
+
+
+def ssd_inputs(torch, dev, b, l, h, p, g, n, seed=2000):
+    gen = torch.Generator().manual_seed(seed)
+    bf = torch.bfloat16
+    return dict(x=torch.randn(b, l, h, p, generator=gen).to(bf).to(dev),
+                dt=(torch.randn(b, l, h, generator=gen) * 0.1 - 4.0).to(dev),
+                A=(-(1.0 + 15.0 * torch.rand(h, generator=gen))).to(dev),
+                B=torch.randn(b, l, g, n, generator=gen).to(bf).to(dev),
+                C=torch.randn(b, l, g, n, generator=gen).to(bf).to(dev),
+                D=torch.randn(h, generator=gen).to(dev),
+                z=torch.randn(b, l, h, p, generator=gen).to(bf).to(dev),
+                dt_bias=(torch.rand(h, generator=gen) * 0.5).to(dev))
+
+
+def ssd_bytes(b, l, h, p, g, n):
+    """Algorithmic bytes of one forward: x, z read and out written (bf16), dt read (fp32), B and C read
+    (bf16), per-head parameters."""
+    return b * l * h * p * 2 * 3 + b * l * h * 4 + 2 * b * l * g * n * 2 + 4 * 3 * h
+
+
+def ssd_cpu_baseline(budget_s):
+    """The reference has no SSD scan; its CPU path for this computation is its Mamba-1 kernel on the
+    equivalent problem (channels = heads x headdim, A repeated over dstate, dt repeated over headdim),
+    timed on a bounded slice of heads with all host threads."""
+    import torch
+
+    import oracle
+    from oracle import f64, ref_c
+
+    cores = _host_cores()
+    torch.set_num_threads(cores)
+    b, l, h, p, g, n = (SSD[k] for k in ("batch", "seqlen", "nheads", "headdim", "ngroups", "dstate"))
+    hs = 2  # heads in the sample
+    x = ssd_inputs(torch, torch.device("cpu"), b, l, hs, p, g, n)
+    f = {k: v.float() for k, v in x.items()}
+    d = hs * p
+    u = f["x"].permute(0, 2, 3, 1).reshape(b, d, l).contiguous()
+    z = f["z"].permute(0, 2, 3, 1).reshape(b, d, l).contiguous()
+    dl = f["dt"].permute(0, 2, 1)[:, :, None, :].expand(b, hs, p, l).reshape(b, d, l).contiguous()
+    A = f["A"][:, None, None].expand(hs, p, n).reshape(d, n).contiguous()
+    D = f["D"][:, None].expand(hs, p).reshape(d).contiguous()
+    bias = f["dt_bias"][:, None].expand(hs, p).reshape(d).contiguous()
+    Bk, Ck = f["B"].reshape(b, l, g, n).permute(0, 2, 1, 3).contiguous(), f["C"].reshape(b, l, g, n).permute(
+        0, 2, 1, 3).contiguous()
+    out, last = torch.empty(b, d, l), torch.empty(b, d, n)
+    P = lambda t: t.data_ptr()  # noqa: E731
+    if oracle.ref_available():
+        kind = "reference"
+
+        def step():
+            ref_c.selective_scan_fwd_f32(P(u), P(dl), P(A), P(Bk), P(Ck), P(D), P(z), P(bias), P(out), P(last),
+                                         b, d, l, n, g, True, cores)
+    else:
+        kind = "port"
+        f64.set_num_threads(cores)
+
+        def step():
+            f64.ssd_fwd(x["x"], x["dt"], x["A"], x["B"], x["C"], x["D"], x["z"], x["dt_bias"], dt_softplus=True)
+    t0 = time.perf_counter()
+    step()
+    first = time.perf_counter() - t0
+    iters = max(1, min(5, int(budget_s / max(first, 1e-3))))
+    t0 = time.perf_counter()
+    for _ in range(iters):
+        step()
+    dt = (time.perf_counter() - t0) / iters
+    return {"value": b * l * d / dt, "unit": "elements/s", "cores": cores, "kind": kind,
+            "sample": f"{iters} timed forward passes (after 1 warm-up) of {hs} of the {h} heads (b={b}, l={l}, "
+                      f"headdim {p}, dstate {n}) through the reference's selective_scan_fwd_f32 on the equivalent "
+                      f"Mamba-1 problem ({d} channels), {cores} threads, time.perf_counter",
+            "ms_per_step": dt * 1e3}
+
+
+def ssd_timing(args, ctx, peak, peak_kind):
+    """Device-timed Mamba-2 SSD forward at the SSD shape (one GPU)."""
+    torch, dev = ctx["torch"], ctx["dev"]
+    from mamba_cpu_b200 import _lib
+    import mamba_cpu_b200 as mb
+
+    b, l, h, p, g, n = (SSD[k] for k in ("batch", "seqlen", "nheads", "headdim", "ngroups", "dstate"))
+    x = ssd_inputs(torch, dev, b, l, h, p, g, n)
+
+    def run():
+        return mb.mamba_chunk_scan_combined(x["x"], x["dt"], x["A"], x["B"], x["C"], 256, D=x["D"], z=x["z"],
+                                            dt_bias=x["dt_bias"], dt_softplus=True)
+    for _ in range(max(3, args.warmup)):
+        run()
+    launches = _lib.last_launch_count()
+    torch.cuda.synchronize(dev)
+    steps = max(args.steps, 20)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    stream = torch.cuda.current_stream(dev)
+    with Clocks(ctx["local"]) as clk:
+        for e0, e1 in evs:
+            e0.record(stream)
+            run()
+            e1.record(stream)
+        torch.cuda.synchronize(dev)
+    ms = sum(e0.elapsed_time(e1) for e0, e1 in evs) / steps
+    E = b * l * h * p
+    nbytes = ssd_bytes(b, l, h, p, g, n)
+    return {
+        "workload": SSD["desc"], "value": E / (ms * 1e-3), "unit": "elements/s",
+        "element": "(batch, timestep, head channel): b * seqlen * nheads * headdim",
+        "tokens_per_s": b * l / (ms * 1e-3), "ms_per_step": ms, "steps": steps,
+        "l2": "inputs larger than L2 (x, z, out 84 MB each): no flush between steps",
+        "roofline": dict(roofline_block("ssd", "ssd_fwd_kernel", nbytes, ms, peak, peak_kind,
+                                        load_traffic("ssd").get("fwd_bytes_per_element"), E),
+                         traffic_source="profiles/roofline_traffic.txt: ncu dram__bytes_read.sum + "
+                                        "dram__bytes_write.sum of ssd_fwd_kernel at this shape "
+                                        "(profiles/ssd_chunk_scan_fwd.md) per element, times the elements"),
+        "gpu_launches": launches * steps, "clocks": clk.summary(),
+    }
+
+
 def run_ours(args):
     import datetime
 
@@ -721,13 +843,16 @@ def run_ours(args):
     if world == 1 and not args.no_models:
         for name in ("c3", "c4"):
             models[name] = model_timing(name, args, ctx)
+    peak, peak_kind = load_peak()
+    ssd = None
+    if world == 1 and not args.no_ssd:
+        ssd = ssd_timing(args, ctx, peak, peak_kind)
     if group is not None:
         dist.barrier()
         dist.destroy_process_group()
     if rank != 0:
         return
 
-    peak, peak_kind = load_peak()
     s = 4 if dt_name == "f32" else 2
     per = D // world
     E_rank = b * per * l
@@ -799,6 +924,10 @@ def run_ours(args):
         if not args.no_cpu_baseline:
             line["c2"]["cpu_baseline"] = cpu_baseline(CONFIGS["c2"], args.cpu_budget)
     line.update(models)
+    if ssd is not None:
+        if not args.no_cpu_baseline:
+            ssd["cpu_baseline"] = ssd_cpu_baseline(args.cpu_budget)
+        line["ssd"] = ssd
     print(json.dumps(line), flush=True)
 
 
@@ -814,6 +943,7 @@ def main():
     p.add_argument("--no-c2", action="store_true", help="skip the config-2 block of the N=1 line")
     p.add_argument("--no-models", action="store_true",
                    help="skip the model-level config-3 / config-4 blocks of the N=1 line")
+    p.add_argument("--no-ssd", action="store_true", help="skip the Mamba-2 SSD block of the N=1 line")
     p.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU baseline work")
     args = p.parse_args()
     if args.warmup < 3:
