@@ -1,7 +1,7 @@
 // ssd.cu -- Mamba-2 SSD chunk scan forward (mamba_chunk_scan_combined) on sm_100a tensor cores.
 //
 // Per (batch, head) the state is a headdim x dstate matrix with one scalar decay per step, so a
-// chunk of Q = 128 steps is four small matrix products (the SSD chunk form of the recurrence,
+// chunk of Q = 64 steps is four small matrix products (the SSD chunk form of the recurrence,
 // Dao & Gu 2024, "Transformers are SSMs", section 6):
 //   G      = C B^T                          (Q x Q)           scores of step i against step j
 //   M      = G o L,  L[i, j] = exp(cs_i - cs_j) dt_j  (j <= i), 0 above the diagonal
@@ -10,29 +10,31 @@
 // with cs the inclusive cumulative sum of dt A inside the chunk. The chunks of a (batch, head)
 // are walked in order by one CTA, which carries S (float32, in registers) from chunk to chunk;
 // CTAs split headdim into 32-wide tiles (S's columns are independent), so the grid is
-// batch x nheads x headdim / 32.
+// batch x nheads x headdim / 32. A CTA is small (128 threads, ~53 KB of shared memory, 128 TMEM
+// columns) so that four fit on an SM and a whole Mamba-2 layer's grid is resident at once.
 //
 // Tensor cores: every product is one tcgen05.mma (kind::f16, bf16 operands, float32 accumulators
-// in Tensor Memory, M = 128) issued by one thread, operands in shared memory in the no-swizzle
-// core-matrix layout (8 rows x 16 bytes per 128-byte core matrix), completion signalled on an
-// mbarrier by tcgen05.commit. The bf16 copy of S that feeds C S^T is split in two (S = hi + lo,
-// both bf16), so the carried state enters the product with ~16 significant bits; M and X' are
-// rounded to bf16 once.
+// in Tensor Memory) issued by one thread, operands in shared memory in the no-swizzle core-matrix
+// layout (8 rows x 16 bytes per 128-byte core matrix), completion signalled on an mbarrier by
+// tcgen05.commit. G, C S^T and M X have M = 64 (row m of the accumulator in TMEM lane
+// (m % 16) + 32 (m / 16), i.e. lanes 0-15 of each warp's quarter); X'^T B has M = 128 (row n in
+// lane n). The bf16 copy of S that feeds C S^T is split in two (S = hi + lo, both bf16), so the
+// carried state enters the product with ~16 significant bits; M and X' are rounded to bf16 once.
 //
-// Shared memory (PT = 32 headdim columns per CTA, 98 KB, two CTAs per SM). Every tile is stored
-// as [column piece c8][row r][8 elements]: 16 bytes per (row, 8 columns), so core matrix
-// (r / 8, c8) -- 8 rows x 16 bytes -- is 128 contiguous bytes, the rows of one column piece are
-// contiguous, and the same bytes serve as a K-major operand (rows = M / N) or an MN-major one
-// (rows = K). A 5-D TMA tensor map per input (8 elements, seqlen, column pieces, group / head,
-// batch) writes exactly this order, so one bulk tensor copy loads a tile; rows past seqlen are
-// zero-filled by the copy.
-//   sCM  [16][128 t]     C tile, then (once C B^T and C S^T are done) M [128 i][128 j]
-//   sB   [16][128 t]     B tile; K-major operand of C B^T, MN-major operand of X'^T B
-//   sX   [PT/8][128 t]   X tile (MN-major operand of M X)
-//   sXs  [PT/8][128 t]   X' (MN-major operand of X'^T B)
-//   sSh, sSl [PT/8][128 n]  bf16 hi / lo parts of S (MN-major operand of C S^T)
+// Shared memory (PT = 32 headdim columns per CTA). Every tile is stored as [column piece c8][row
+// r][8 elements]: 16 bytes per (row, 8 columns), so core matrix (r / 8, c8) -- 8 rows x 16 bytes
+// -- is 128 contiguous bytes, the rows of one column piece are contiguous, and the same bytes
+// serve as a K-major operand (rows = M / N) or an MN-major one (rows = K). A 5-D TMA tensor map
+// per input (8 elements, seqlen, column pieces, group / head, batch) writes exactly this order, so
+// one bulk tensor copy loads a tile; rows past seqlen are zero-filled by the copy.
+//   sCM  [16][64 t]      C tile, then (once C B^T and C S^T are done) M [64 i][64 j] in its
+//                        first 8 pieces
+//   sB   [16][64 t]      B tile; K-major operand of C B^T, MN-major operand of X'^T B
+//   sX   [PT/8][64 t]    X tile (MN-major operand of M X)
+//   sSh, sSl [PT/8][128 n]  bf16 hi / lo parts of S (MN-major operand of C S^T); X' [PT/8][64 t]
+//                        reuses sSl once C S^T is done
 // dstate is zero-padded to 128 (the padded columns of B stay zero, so S's padded rows stay zero).
-// TMEM (256 columns): [0, 128) G, then M X; [128, 128 + PT) C S^T; [128 + PT, 128 + 2 PT) X'^T B.
+// TMEM (128 columns): [0, 64) G, then M X in [0, PT); [64, 64 + PT) C S^T; [96, 128) X'^T B.
 // The chunk's tiles are copied in while the previous chunk's outputs are written: the copies for
 // chunk k + 1 are issued as soon as chunk k's last products have completed.
 #include <cuda.h>
@@ -46,11 +48,11 @@ namespace mb200 {
 
 namespace {
 
-constexpr int kQ = 128;        // steps per chunk (the M of every product)
+constexpr int kQ = 64;         // steps per chunk
 constexpr int kNP = 128;       // dstate padded
 constexpr int kPT = 32;        // headdim columns per CTA
-constexpr int kSsdThreads = 256;
-constexpr uint32_t kSsdTmemCols = 256;
+constexpr int kSsdThreads = 128;
+constexpr uint32_t kSsdTmemCols = 128;
 
 constexpr int kTileCM = kQ * kNP * 2;   // bytes
 constexpr int kTileB = kQ * kNP * 2;
@@ -58,9 +60,9 @@ constexpr int kTileX = kQ * kPT * 2;
 constexpr int kTileS = kNP * kPT * 2;
 constexpr int kOffB = kTileCM;
 constexpr int kOffX = kOffB + kTileB;
-constexpr int kOffXs = kOffX + kTileX;
-constexpr int kOffSh = kOffXs + kTileX;
+constexpr int kOffSh = kOffX + kTileX;
 constexpr int kOffSl = kOffSh + kTileS;
+constexpr int kOffXs = kOffSl;                     // X' reuses the lo part of S
 constexpr int kOffF = kOffSl + kTileS;             // float area
 constexpr int kFloats = 2 * kQ + 8 + kPT;          // dt, cs, warp sums, D
 constexpr int kOffBar = kOffF + kFloats * 4;
@@ -85,8 +87,8 @@ struct SsdArgs {
   int ntiles;  // P / kPT
 };
 
-// Byte offset of the 16-byte piece (row r, column piece c8 = column / 8) of a 128-row tile.
-__device__ __forceinline__ uint32_t core16(int r, int c8) { return (uint32_t)((c8 * kQ + r) * 16); }
+// Byte offset of the 16-byte piece (row r, column piece c8 = column / 8) of a tile with `rows` rows.
+__device__ __forceinline__ uint32_t core16(int r, int c8, int rows = kQ) { return (uint32_t)((c8 * rows + r) * 16); }
 
 // Shared-memory matrix descriptor, no swizzle (sm_100 version 1): start address, leading byte
 // offset (between core matrices adjacent along K) and stride byte offset (between core matrices
@@ -170,15 +172,14 @@ struct SsdMaps {
   CUtensorMap B, C, x;
 };
 
-// Thread roles (256 threads): row = tid % 128 is the thread's accumulator row (TMEM lane; warps w
-// and w + 4 share lanes 32 (w % 4) .. + 31) and half = tid / 128 picks its half of the columns:
-// headdim columns [16 half, 16 half + 16) of the outputs and of S, and the 16-wide column pieces
-// q with q % 2 == half of M (so both halves of a row get the same number of non-zero pieces).
-__global__ void __launch_bounds__(kSsdThreads, 2) ssd_fwd_kernel(SsdArgs a, const __grid_constant__ SsdMaps maps) {
+// Thread roles (128 threads, 4 warps): S row n = tid (TMEM lane n of X'^T B). The 64-row
+// accumulators live in lanes 0-15 of each warp's quarter, so lane l < 16 of warp w owns chunk row
+// i = 16 w + l (masked decay matrix, outputs) and lane l >= 16 owns row 16 w + l - 16 of X'.
+__global__ void __launch_bounds__(kSsdThreads, 4) ssd_fwd_kernel(SsdArgs a, const __grid_constant__ SsdMaps maps) {
   extern __shared__ __align__(1024) uint8_t smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int row = tid & (kQ - 1), half = tid >> 7, rw = warp & 3;
-  constexpr int kPH = kPT / 2;  // headdim columns per half
+  const bool lo16 = lane < 16;
+  const int crow = 16 * warp + (lane & 15);  // this thread's chunk row (M phase, outputs or X')
   const int tile = blockIdx.x % a.ntiles;
   const int64_t bh = blockIdx.x / a.ntiles;
   const int64_t h = bh % a.H, b = bh / a.H;
@@ -202,67 +203,74 @@ __global__ void __launch_bounds__(kSsdThreads, 2) ssd_fwd_kernel(SsdArgs a, cons
   const uint32_t tile_bytes = (uint32_t)(2 * kQ * 16 * nc8 + kTileX);
 
   if (warp == 0) tmem_alloc(tslot, kSsdTmemCols);
-  // zero the padded dstate columns of B (the copies never write them)
+  // zero the padded dstate columns of B and C (the copies never write them; M overwrites C's
+  // first 8 pieces, which are re-zeroed where needed in the chunk loop)
   for (int i = tid; i < kQ * 16; i += kSsdThreads) {
-    const int r = i & (kQ - 1), c8 = i >> 7;
-    if (c8 >= nc8) *reinterpret_cast<uint4*>(smem + kOffB + core16(r, c8)) = make_uint4(0, 0, 0, 0);
+    const int r = i & (kQ - 1), c8 = i / kQ;
+    if (c8 >= nc8) {
+      *reinterpret_cast<uint4*>(smem + kOffB + core16(r, c8)) = make_uint4(0, 0, 0, 0);
+      *reinterpret_cast<uint4*>(smem + core16(r, c8)) = make_uint4(0, 0, 0, 0);
+    }
   }
   if (tid == 0) {
     mbar_init(bar, 1);
     mbar_init(tbar, 1);
     mbar_fence_init();
-    if (nchunks > 0) {
-      mbar_arrive_expect_tx(tbar, tile_bytes);
-      tma_load_5d(sCM, &maps.C, 0, 0, 0, (int)g, (int)b, tbar);
-      tma_load_5d(sB, &maps.B, 0, 0, 0, (int)g, (int)b, tbar);
-      tma_load_5d(sX, &maps.x, 0, 0, p0 / 8, (int)h, (int)b, tbar);
-    }
+  }
+  fence_proxy_async();  // the zeroed pieces before the first copy and product
+  __syncthreads();
+  if (tid == 0 && nchunks > 0) {
+    mbar_arrive_expect_tx(tbar, tile_bytes);
+    tma_load_5d(sCM, &maps.C, 0, 0, 0, (int)g, (int)b, tbar);
+    tma_load_5d(sB, &maps.B, 0, 0, 0, (int)g, (int)b, tbar);
+    tma_load_5d(sX, &maps.x, 0, 0, p0 / 8, (int)h, (int)b, tbar);
   }
   if (tid < kPT) {
     float dv = 0.f;
     if (a.D != nullptr) dv = a.D_per_dim ? a.D[h * a.P + p0 + tid] : a.D[h];
     sD[tid] = dv;
   }
-  // S row n = row, columns [kPH half, + kPH) (float32): initial state or zeros
-  float S[kPH];
+  // S row n = tid (float32): initial state or zeros
+  float S[kPT];
 #pragma unroll
-  for (int p = 0; p < kPH; ++p)
-    S[p] = (a.init != nullptr && row < N) ? a.init[((b * a.H + h) * a.P + p0 + kPH * half + p) * a.N + row] : 0.f;
+  for (int p = 0; p < kPT; ++p)
+    S[p] = (a.init != nullptr && tid < N) ? a.init[((b * a.H + h) * a.P + p0 + p) * a.N + tid] : 0.f;
   const float A2 = a.A[h] * kLog2e;
   const float bias = a.dt_bias != nullptr ? a.dt_bias[h] : 0.f;
-  const __nv_bfloat16* zbase = a.z != nullptr ? a.z + b * a.zbs + h * a.zhs + p0 + kPH * half : nullptr;
+  const __nv_bfloat16* zbase = a.z != nullptr ? a.z + b * a.zbs + h * a.zhs + p0 : nullptr;
   const float* dtbase = a.dt + b * a.dtbs + h;
 
   tmem_fence_before_sync();
   __syncthreads();
   tmem_fence_after_sync();
   const uint32_t tbase = *tslot;
-  const uint32_t trow = tbase + ((uint32_t)(rw * 32) << 16);  // this warp's lanes
+  const uint32_t trow = tbase + ((uint32_t)(warp * 32) << 16);  // this warp's lanes
 
   constexpr uint32_t kIdG = idesc_bf16(kQ, kQ, 0, 0);
   constexpr uint32_t kIdY = idesc_bf16(kQ, kPT, 0, 1);
   constexpr uint32_t kIdS = idesc_bf16(kNP, kPT, 1, 1);
-  // Column-piece-major tiles: core matrices 128 bytes apart along the rows, kQ * 16 bytes apart
-  // along the column pieces. K-major (rows = M / N): LBO = piece stride, SBO = 128; MN-major
-  // (rows = K): LBO = 128, SBO = piece stride. A K step of 16 is two pieces (K-major) or two
-  // 8-row groups (MN-major).
-  constexpr uint32_t kPiece = kQ * 16;
+  // Column-piece-major tiles: core matrices 128 bytes apart along the rows, rows * 16 bytes
+  // apart along the column pieces. K-major (rows = M / N): LBO = piece stride, SBO = 128;
+  // MN-major (rows = K): LBO = 128, SBO = piece stride. A K step of 16 is two pieces (K-major)
+  // or two 8-row groups (MN-major).
+  constexpr uint32_t kPiece = kQ * 16;     // 64-row tiles (C, B, M, X, X')
+  constexpr uint32_t kPieceS = kNP * 16;   // 128-row tiles (S)
   constexpr uint32_t kColYo = kQ, kColSl = kQ + kPT;
 
   uint32_t phase = 0, tphase = 0;
-  float dt_raw = (half == 0 && row < a.L) ? dtbase[row * a.dtls] : 0.f;
+  float dt_raw = (tid < kQ && tid < a.L) ? dtbase[tid * a.dtls] : 0.f;
   for (int64_t k = 0; k < nchunks; ++k) {
     const int64_t t0 = k * kQ;
     const int valid = (int)(a.L - t0 < kQ ? a.L - t0 : kQ);
 
-    // ---- S_prev as bf16 hi + lo, this chunk's z (registers), dt and its cumulative sum
-    uint4 zv[kPH / 8];
-    if (zbase != nullptr && row < valid) {
+    // ---- S_prev as bf16 hi + lo (row n = tid), this chunk's z (registers), dt and its sums
+    uint4 zv[kPT / 8];
+    if (lo16 && zbase != nullptr && crow < valid) {
 #pragma unroll
-      for (int c = 0; c < kPH / 8; ++c) zv[c] = __ldg(reinterpret_cast<const uint4*>(zbase + (t0 + row) * a.zls) + c);
+      for (int c = 0; c < kPT / 8; ++c) zv[c] = __ldg(reinterpret_cast<const uint4*>(zbase + (t0 + crow) * a.zls) + c);
     }
 #pragma unroll
-    for (int c = 0; c < kPH / 8; ++c) {
+    for (int c = 0; c < kPT / 8; ++c) {
       uint32_t hi[4], lo[4];
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
@@ -271,21 +279,20 @@ __global__ void __launch_bounds__(kSsdThreads, 2) ssd_fwd_kernel(SsdArgs a, cons
         const float2 hv = unpack_bf16(hi[q]);
         lo[q] = pack_bf16(v0 - hv.x, v1 - hv.y);
       }
-      const uint32_t off = core16(row, (kPH / 8) * half + c);
+      const uint32_t off = core16(tid, c, kNP);
       *reinterpret_cast<uint4*>(smem + kOffSh + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
       *reinterpret_cast<uint4*>(smem + kOffSl + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
     }
-    if ((nc8 & 1) && half == 1)  // C columns [dstate, dstate + 8) of the last K step (M overwrote them)
-      *reinterpret_cast<uint4*>(smem + core16(row, nc8)) = make_uint4(0, 0, 0, 0);
-    float cs = 0.f;
-    if (half == 0) {
+    if ((nc8 & 1) && nc8 < 8 && tid < kQ)  // C columns [dstate, dstate + 8) of the last K step (M overwrote them)
+      *reinterpret_cast<uint4*>(smem + core16(tid, nc8)) = make_uint4(0, 0, 0, 0);
+    if (tid < kQ) {  // warps 0 and 1: dt (softplus, clamp) and the cumulative sum of dt A
       float dtv = 0.f;
-      if (row < valid) {
+      if (tid < valid) {
         float raw = dt_raw + bias;
         if (a.softplus) raw = softplus_f(raw);
         dtv = fminf(fmaxf(raw, a.dt_min), a.dt_max);
       }
-      sdt[row] = dtv;
+      sdt[tid] = dtv;
       float v = dtv * A2;  // log2 units
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
@@ -293,22 +300,18 @@ __global__ void __launch_bounds__(kSsdThreads, 2) ssd_fwd_kernel(SsdArgs a, cons
         if (lane >= o) v += u;
       }
       if (lane == 31) swarp[warp] = v;
-      cs = v;
-      // the next chunk's dt (its latency overlaps this chunk)
-      dt_raw = (t0 + kQ + row < a.L) ? dtbase[(t0 + kQ + row) * a.dtls] : 0.f;
+      scs[tid] = v;  // warp-inclusive; warp 1 adds warp 0's total below
+      dt_raw = (t0 + kQ + tid < a.L) ? dtbase[(t0 + kQ + tid) * a.dtls] : 0.f;  // the next chunk's
     }
     __syncthreads();
-    if (half == 0) {
-      for (int w = 0; w < rw; ++w) cs += swarp[w];
-      scs[row] = cs;
-    }
+    if (tid >= 32 && tid < kQ) scs[tid] += swarp[0];
     mbar_wait_spin(tbar, tphase);  // this chunk's tiles have landed
     tphase ^= 1;
     fence_proxy_async();
     tmem_fence_before_sync();
     __syncthreads();
     const float cs_end = scs[kQ - 1];
-    cs = scs[row];
+    const float cs = scs[crow];
 
     // ---- G = C B^T and Yo = C S^T (hi, then lo)
     if (tid == 0) {
@@ -317,10 +320,10 @@ __global__ void __launch_bounds__(kSsdThreads, 2) ssd_fwd_kernel(SsdArgs a, cons
         umma_bf16(tbase, sdesc(sCM + s * 2 * kPiece, kPiece, 128), sdesc(sB + s * 2 * kPiece, kPiece, 128), kIdG,
                   s > 0);
       for (int s = 0; s < ksteps; ++s)
-        umma_bf16(tbase + kColYo, sdesc(sCM + s * 2 * kPiece, kPiece, 128), sdesc(sSh + s * 256, 128, kPiece), kIdY,
+        umma_bf16(tbase + kColYo, sdesc(sCM + s * 2 * kPiece, kPiece, 128), sdesc(sSh + s * 256, 128, kPieceS), kIdY,
                   s > 0);
       for (int s = 0; s < ksteps; ++s)
-        umma_bf16(tbase + kColYo, sdesc(sCM + s * 2 * kPiece, kPiece, 128), sdesc(sSl + s * 256, 128, kPiece), kIdY,
+        umma_bf16(tbase + kColYo, sdesc(sCM + s * 2 * kPiece, kPiece, 128), sdesc(sSl + s * 256, 128, kPieceS), kIdY,
                   1);
       umma_commit(bar);
     }
@@ -328,15 +331,14 @@ __global__ void __launch_bounds__(kSsdThreads, 2) ssd_fwd_kernel(SsdArgs a, cons
     phase ^= 1;
     tmem_fence_after_sync();
 
-    // ---- M = G o L over C's tile (row i, pieces q % 2 == half), X' = w X (this half's columns)
-    uint4 xv[kPH / 8];  // this row's x, kept for the output stage (the next chunk's copy reuses sX)
+    // ---- lanes < 16: M = G o L (row i = crow) over C's tile; lanes >= 16: X' = w X (row crow)
+    uint4 xv[kPT / 8];  // lanes < 16: this row's x, kept for the output stage
     {
-      const int i = row;
-      const int nz = 2 * rw + 2;  // pieces of this warp's rows that reach the diagonal
+      const int i = crow;
 #pragma unroll 1
-      for (int q = half; q < kQ / 16; q += 2) {
+      for (int q = 0; q < kQ / 16; ++q) {
         uint4 w0 = make_uint4(0, 0, 0, 0), w1 = make_uint4(0, 0, 0, 0);
-        if (q < nz) {  // warp-uniform
+        if (q <= warp) {  // warp-uniform: rows 16 warp .. + 15 reach column 16 q
           float gv[16];
           tmem_ld16(trow + q * 16, gv);
           tmem_wait_ld();
@@ -356,22 +358,26 @@ __global__ void __launch_bounds__(kSsdThreads, 2) ssd_fwd_kernel(SsdArgs a, cons
           w0 = make_uint4(pk[0], pk[1], pk[2], pk[3]);
           w1 = make_uint4(pk[4], pk[5], pk[6], pk[7]);
         }
-        *reinterpret_cast<uint4*>(smem + core16(i, 2 * q)) = w0;
-        *reinterpret_cast<uint4*>(smem + core16(i, 2 * q + 1)) = w1;
+        if (lo16) {
+          *reinterpret_cast<uint4*>(smem + core16(i, 2 * q)) = w0;
+          *reinterpret_cast<uint4*>(smem + core16(i, 2 * q + 1)) = w1;
+        }
       }
       const float wx = ex2(cs_end - cs) * sdt[i];
 #pragma unroll
-      for (int c = 0; c < kPH / 8; ++c) {
-        const uint32_t off = core16(i, (kPH / 8) * half + c);
+      for (int c = 0; c < kPT / 8; ++c) {
+        const uint32_t off = core16(i, c);
         xv[c] = *reinterpret_cast<const uint4*>(smem + kOffX + off);
-        const uint32_t in[4] = {xv[c].x, xv[c].y, xv[c].z, xv[c].w};
-        uint32_t o[4];
+        if (!lo16) {
+          const uint32_t in[4] = {xv[c].x, xv[c].y, xv[c].z, xv[c].w};
+          uint32_t o[4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 f = unpack_bf16(in[e]);
-          o[e] = pack_bf16(f.x * wx, f.y * wx);
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = unpack_bf16(in[e]);
+            o[e] = pack_bf16(f.x * wx, f.y * wx);
+          }
+          *reinterpret_cast<uint4*>(smem + kOffXs + off) = make_uint4(o[0], o[1], o[2], o[3]);
         }
-        *reinterpret_cast<uint4*>(smem + kOffXs + off) = make_uint4(o[0], o[1], o[2], o[3]);
       }
     }
     fence_proxy_async();
@@ -398,30 +404,33 @@ __global__ void __launch_bounds__(kSsdThreads, 2) ssd_fwd_kernel(SsdArgs a, cons
       tma_load_5d(sX, &maps.x, 0, tn, p0 / 8, (int)h, (int)b, tbar);
     }
 
-    // ---- outputs of row i, columns [kPH half, + kPH), and the carried state (row n = row)
-    {
-      float yo[kPH], yd[kPH], sl[kPH];
-      const uint32_t cb = kPH * half;
-      tmem_ld16(trow + kColYo + cb, yo);
-      tmem_ld16(trow + cb, yd);
-      tmem_ld16(trow + kColSl + cb, sl);
-      tmem_wait_ld();
-      const int i = row;
-      if (i < valid) {
-        const float eo = ex2(cs);
-        const int64_t t = t0 + i;
-        __nv_bfloat16* orow = a.out + ((b * a.L + t) * a.H + h) * a.P + p0 + cb;
+    // ---- outputs of row crow (lanes < 16), in two halves of 16 columns
 #pragma unroll
-        for (int c = 0; c < kPH / 8; ++c) {
-          const uint32_t xin[4] = {xv[c].x, xv[c].y, xv[c].z, xv[c].w};
-          const uint32_t zin[4] = {zv[c].x, zv[c].y, zv[c].z, zv[c].w};
+    for (int hf = 0; hf < 2; ++hf) {
+      float yo[16], yd[16];
+      tmem_ld16(trow + kColYo + 16 * hf, yo);
+      tmem_ld16(trow + 16 * hf, yd);
+      tmem_wait_ld();
+      if (lo16 && crow < valid) {
+        const float eo = ex2(cs);
+        const int64_t t = t0 + crow;
+        __nv_bfloat16* orow = a.out + ((b * a.L + t) * a.H + h) * a.P + p0 + 16 * hf;
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const uint4 xq = xv[2 * hf + c];
+          const uint32_t xin[4] = {xq.x, xq.y, xq.z, xq.w};
+          uint32_t zin[4] = {0, 0, 0, 0};
+          if (zbase != nullptr) {
+            const uint4 zq = zv[2 * hf + c];
+            zin[0] = zq.x, zin[1] = zq.y, zin[2] = zq.z, zin[3] = zq.w;
+          }
           uint32_t o[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const int p = c * 8 + 2 * e;
             const float2 xf = unpack_bf16(xin[e]);
-            float y0 = fmaf(eo, yo[p], yd[p]) + sD[cb + p] * xf.x;
-            float y1 = fmaf(eo, yo[p + 1], yd[p + 1]) + sD[cb + p + 1] * xf.y;
+            float y0 = fmaf(eo, yo[p], yd[p]) + sD[16 * hf + p] * xf.x;
+            float y1 = fmaf(eo, yo[p + 1], yd[p + 1]) + sD[16 * hf + p + 1] * xf.y;
             if (zbase != nullptr) {
               const float2 zf = unpack_bf16(zin[e]);
               y0 *= silu_f(zf.x);
@@ -432,17 +441,26 @@ __global__ void __launch_bounds__(kSsdThreads, 2) ssd_fwd_kernel(SsdArgs a, cons
           *reinterpret_cast<uint4*>(orow + c * 8) = make_uint4(o[0], o[1], o[2], o[3]);
         }
       }
+    }
+    // ---- the carried state (row n = tid)
+    {
       const float decay = ex2(cs_end);
+      float sl[16];
 #pragma unroll
-      for (int p = 0; p < kPH; ++p) S[p] = fmaf(decay, S[p], sl[p]);
+      for (int hf = 0; hf < 2; ++hf) {
+        tmem_ld16(trow + kColSl + 16 * hf, sl);
+        tmem_wait_ld();
+#pragma unroll
+        for (int p = 0; p < 16; ++p) S[16 * hf + p] = fmaf(decay, S[16 * hf + p], sl[p]);
+      }
     }
     tmem_fence_before_sync();
     __syncthreads();
   }
 
-  if (a.final_states != nullptr && row < N) {
+  if (a.final_states != nullptr && tid < N) {
 #pragma unroll
-    for (int p = 0; p < kPH; ++p) a.final_states[((b * a.H + h) * a.P + p0 + kPH * half + p) * a.N + row] = S[p];
+    for (int p = 0; p < kPT; ++p) a.final_states[((b * a.H + h) * a.P + p0 + p) * a.N + tid] = S[p];
   }
   tmem_fence_before_sync();
   __syncthreads();
