@@ -127,9 +127,10 @@ __device__ __forceinline__ float2 unpack_bf16(uint32_t w) {
   return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w));
 }
 
-// Wait for the mbarrier phase with the given parity (tensor-core completion): a tight try_wait
-// loop, bounded by 2 s of GPU time (%globaltimer); on timeout the fault word records it and the
-// kernel carries on.
+// Wait for the mbarrier phase with the given parity (tensor-core or copy completion): try_wait
+// with a suspend-time hint, so a waiting warp sleeps (and leaves its issue slots to the other
+// CTAs of the SM) until the phase completes; bounded by 2 s of GPU time (%globaltimer). On timeout
+// the fault word records it and the kernel carries on.
 __device__ __forceinline__ uint64_t global_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -137,22 +138,16 @@ __device__ __forceinline__ uint64_t global_ns() {
 }
 __device__ __forceinline__ void mbar_wait_spin(uint64_t* bar, uint32_t parity) {
   const uint32_t addr = smem_u32(bar);
-  uint64_t t_start = 0;
-  for (uint32_t i = 0;; ++i) {
+  const uint64_t t_start = global_ns();
+  for (;;) {
     uint32_t done;
     asm volatile(
-        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\tselp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(done)
-        : "r"(addr), "r"(parity)
+        : "r"(addr), "r"(parity), "r"(1000000u)
         : "memory");
     if (done) return;
-    if ((i & 1023u) == 0) {
-      const uint64_t t = global_ns();
-      if (i == 0)
-        t_start = t;
-      else if (t - t_start > 2000000000ull)
-        break;
-    }
+    if (global_ns() - t_start > 2000000000ull) break;
   }
   atomicOr(&g_mb200_fault, kFaultWaitTimeout);
 }

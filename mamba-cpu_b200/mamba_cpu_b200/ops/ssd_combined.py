@@ -12,7 +12,7 @@ per step,
 This is the Mamba-1 selective scan of ``selective_scan_fn`` with channels = nheads * headdim, A
 broadcast over dstate and delta broadcast over headdim, which is how the tests pin it to the
 reference's own kernel. The work runs in one sm_100a kernel (``mb200_ssd_chunk_scan_fwd`` in
-libmamba_b200.so): 128-step chunks as tcgen05 matrix products, the state carried in float32.
+libmamba_b200.so): 64-step chunks as tcgen05 matrix products, the state carried in float32.
 """
 
 import math
@@ -124,7 +124,7 @@ def mamba_chunk_scan_combined(
     dt is clamped to ``dt_limit`` after the bias and the optional softplus (threshold 20), as
     upstream does; the default (0, inf) only removes negative steps. ``chunk_size`` is checked
     and otherwise does not change the result beyond rounding: the kernel always works in chunks
-    of 128 steps. This build takes bf16 x / z (B and C are used in bf16), dstate a multiple of 8
+    of 64 steps. This build takes bf16 x / z (B and C are used in bf16), dstate a multiple of 8
     up to 128 and headdim a multiple of 32 up to 256. ``seq_idx``, ``cu_seqlens`` and
     ``return_varlen_states`` (packed variable-length batches) are not supported, and neither is
     the backward.
