@@ -333,6 +333,11 @@ MB200_API int mb200_causal_conv1d_update(const mb200_conv1d_update_params* p, vo
  *   initial_states  : (batch, nheads, headdim, dstate) float32 or NULL (zeros)
  *   final_states    : (batch, nheads, headdim, dstate) float32 or NULL: the state after the last
  *                     step
+ *   seq_idx         : (batch, seqlen) int32, non-decreasing along seqlen, or NULL: packed
+ *                     sequences; no step sees another sequence's steps and the state restarts
+ *                     from zero where the index changes. initial_states belong to sequence 0 (as
+ *                     upstream: they are dropped if seq_idx[b, 0] != 0), final_states are the
+ *                     last sequence's.
  * Limits of this build: x_dtype MB200_BF16, dstate a multiple of 8 up to 128, headdim a multiple
  * of 32 up to 256 (MB200_ERR_UNSUPPORTED otherwise). One kernel launch, no scratch memory.
  */
@@ -354,6 +359,8 @@ typedef struct mb200_ssd_params {
   int64_t B_batch_stride, B_seqlen_stride, B_group_stride;
   int64_t C_batch_stride, C_seqlen_stride, C_group_stride;
   int64_t dt_batch_stride, dt_seqlen_stride;
+  const int32_t* seq_idx;
+  int64_t seq_idx_batch_stride, seq_idx_seqlen_stride;
   float dt_min, dt_max;
   int32_t x_dtype;
   int32_t dt_softplus;

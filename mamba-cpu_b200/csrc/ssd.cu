@@ -64,7 +64,7 @@ constexpr int kOffSh = kOffX + kTileX;
 constexpr int kOffSl = kOffSh + kTileS;
 constexpr int kOffXs = kOffSl;                     // X' reuses the lo part of S
 constexpr int kOffF = kOffSl + kTileS;             // float area
-constexpr int kFloats = 2 * kQ + 8 + kPT;          // dt, cs, warp sums, D
+constexpr int kFloats = 3 * kQ + 8 + kPT;          // dt, cs, sequence ids (int), warp sums, D
 constexpr int kOffBar = kOffF + kFloats * 4;
 constexpr int kSsdSmem = kOffBar + 32;
 
@@ -82,6 +82,8 @@ struct SsdArgs {
   float* final_states;
   int64_t L, H, P, G, N;
   int64_t xbs, xls, xhs, zbs, zls, zhs, Bbs, Bls, Bgs, Cbs, Cls, Cgs, dtbs, dtls;
+  const int32_t* seq_idx;  // (batch, seqlen) or null
+  int64_t sqbs, sqls;
   float dt_min, dt_max;
   int softplus, D_per_dim;
   int ntiles;  // P / kPT
@@ -170,6 +172,8 @@ struct SsdMaps {
 // Thread roles (128 threads, 4 warps): S row n = tid (TMEM lane n of X'^T B). The 64-row
 // accumulators live in lanes 0-15 of each warp's quarter, so lane l < 16 of warp w owns chunk row
 // i = 16 w + l (masked decay matrix, outputs) and lane l >= 16 owns row 16 w + l - 16 of X'.
+// SEQ: packed sequences (seq_idx); the other instantiation drops the sequence masks.
+template <bool SEQ>
 __global__ void __launch_bounds__(kSsdThreads, 4) ssd_fwd_kernel(SsdArgs a, const __grid_constant__ SsdMaps maps) {
   extern __shared__ __align__(1024) uint8_t smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -183,7 +187,8 @@ __global__ void __launch_bounds__(kSsdThreads, 4) ssd_fwd_kernel(SsdArgs a, cons
 
   float* sdt = reinterpret_cast<float*>(smem + kOffF);
   float* scs = sdt + kQ;
-  float* swarp = scs + kQ;
+  int* sseq = reinterpret_cast<int*>(scs + kQ);  // sequence id of each step of the chunk
+  float* swarp = reinterpret_cast<float*>(sseq + kQ);
   float* sD = swarp + 8;
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kOffBar);       // tensor-core completion
   uint64_t* tbar = reinterpret_cast<uint64_t*>(smem + kOffBar + 8);  // tile copies
@@ -252,6 +257,11 @@ __global__ void __launch_bounds__(kSsdThreads, 4) ssd_fwd_kernel(SsdArgs a, cons
   constexpr uint32_t kPieceS = kNP * 16;   // 128-row tiles (S)
   constexpr uint32_t kColYo = kQ, kColSl = kQ + kPT;
 
+  // Packed sequences (seq_idx): the carried state belongs to sequence seq_prev (initial states to
+  // sequence 0, as upstream); a step only sees steps and carried state of its own sequence.
+  const int32_t* seqbase = SEQ ? a.seq_idx + b * a.sqbs : nullptr;
+  int seq_prev = 0;
+
   uint32_t phase = 0, tphase = 0;
   float dt_raw = (tid < kQ && tid < a.L) ? dtbase[tid * a.dtls] : 0.f;
   for (int64_t k = 0; k < nchunks; ++k) {
@@ -288,6 +298,7 @@ __global__ void __launch_bounds__(kSsdThreads, 4) ssd_fwd_kernel(SsdArgs a, cons
         dtv = fminf(fmaxf(raw, a.dt_min), a.dt_max);
       }
       sdt[tid] = dtv;
+      if constexpr (SEQ) sseq[tid] = tid < valid ? seqbase[(t0 + tid) * a.sqls] : -1;
       float v = dtv * A2;  // log2 units
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
@@ -307,6 +318,7 @@ __global__ void __launch_bounds__(kSsdThreads, 4) ssd_fwd_kernel(SsdArgs a, cons
     __syncthreads();
     const float cs_end = scs[kQ - 1];
     const float cs = scs[crow];
+    const int seq_i = SEQ ? sseq[crow] : 0, seq_last = SEQ ? sseq[valid - 1] : 0;
 
     // ---- G = C B^T and Yo = C S^T (hi, then lo)
     if (tid == 0) {
@@ -343,10 +355,11 @@ __global__ void __launch_bounds__(kSsdThreads, 4) ssd_fwd_kernel(SsdArgs a, cons
             const int j = q * 16 + jj;
             const float4 cj = *reinterpret_cast<const float4*>(&scs[j]);
             const float4 dj = *reinterpret_cast<const float4*>(&sdt[j]);
-            const float m0 = j <= i ? gv[jj] * ex2(cs - cj.x) * dj.x : 0.f;
-            const float m1 = j + 1 <= i ? gv[jj + 1] * ex2(cs - cj.y) * dj.y : 0.f;
-            const float m2 = j + 2 <= i ? gv[jj + 2] * ex2(cs - cj.z) * dj.z : 0.f;
-            const float m3 = j + 3 <= i ? gv[jj + 3] * ex2(cs - cj.w) * dj.w : 0.f;
+            const int4 sj = SEQ ? *reinterpret_cast<const int4*>(&sseq[j]) : make_int4(0, 0, 0, 0);
+            const float m0 = (j <= i && sj.x == seq_i) ? gv[jj] * ex2(cs - cj.x) * dj.x : 0.f;
+            const float m1 = (j + 1 <= i && sj.y == seq_i) ? gv[jj + 1] * ex2(cs - cj.y) * dj.y : 0.f;
+            const float m2 = (j + 2 <= i && sj.z == seq_i) ? gv[jj + 2] * ex2(cs - cj.z) * dj.z : 0.f;
+            const float m3 = (j + 3 <= i && sj.w == seq_i) ? gv[jj + 3] * ex2(cs - cj.w) * dj.w : 0.f;
             pk[jj / 2] = pack_bf16(m0, m1);
             pk[jj / 2 + 1] = pack_bf16(m2, m3);
           }
@@ -358,7 +371,8 @@ __global__ void __launch_bounds__(kSsdThreads, 4) ssd_fwd_kernel(SsdArgs a, cons
           *reinterpret_cast<uint4*>(smem + core16(i, 2 * q + 1)) = w1;
         }
       }
-      const float wx = ex2(cs_end - cs) * sdt[i];
+      // X' rows of the chunk's last sequence only: earlier sequences end inside the chunk
+      const float wx = seq_i == seq_last ? ex2(cs_end - cs) * sdt[i] : 0.f;
 #pragma unroll
       for (int c = 0; c < kPT / 8; ++c) {
         const uint32_t off = core16(i, c);
@@ -407,7 +421,7 @@ __global__ void __launch_bounds__(kSsdThreads, 4) ssd_fwd_kernel(SsdArgs a, cons
       tmem_ld16(trow + 16 * hf, yd);
       tmem_wait_ld();
       if (lo16 && crow < valid) {
-        const float eo = ex2(cs);
+        const float eo = seq_i == seq_prev ? ex2(cs) : 0.f;  // the carried state, if it is this row's sequence
         const int64_t t = t0 + crow;
         __nv_bfloat16* orow = a.out + ((b * a.L + t) * a.H + h) * a.P + p0 + 16 * hf;
 #pragma unroll
@@ -439,7 +453,7 @@ __global__ void __launch_bounds__(kSsdThreads, 4) ssd_fwd_kernel(SsdArgs a, cons
     }
     // ---- the carried state (row n = tid)
     {
-      const float decay = ex2(cs_end);
+      const float decay = seq_last == seq_prev ? ex2(cs_end) : 0.f;  // a new sequence starts from zero
       float sl[16];
 #pragma unroll
       for (int hf = 0; hf < 2; ++hf) {
@@ -449,6 +463,7 @@ __global__ void __launch_bounds__(kSsdThreads, 4) ssd_fwd_kernel(SsdArgs a, cons
         for (int p = 0; p < 16; ++p) S[16 * hf + p] = fmaf(decay, S[16 * hf + p], sl[p]);
       }
     }
+    seq_prev = seq_last;
     tmem_fence_before_sync();
     __syncthreads();
   }
@@ -544,6 +559,7 @@ MB200_API int mb200_ssd_chunk_scan_fwd(const mb200_ssd_params* p, void* stream) 
   a.Bbs = p->B_batch_stride, a.Bls = p->B_seqlen_stride, a.Bgs = p->B_group_stride;
   a.Cbs = p->C_batch_stride, a.Cls = p->C_seqlen_stride, a.Cgs = p->C_group_stride;
   a.dtbs = p->dt_batch_stride, a.dtls = p->dt_seqlen_stride;
+  a.seq_idx = p->seq_idx, a.sqbs = p->seq_idx_batch_stride, a.sqls = p->seq_idx_seqlen_stride;
   a.dt_min = p->dt_min, a.dt_max = p->dt_max;
   a.softplus = p->dt_softplus != 0;
   a.D_per_dim = p->D_per_dim != 0;
@@ -557,9 +573,10 @@ MB200_API int mb200_ssd_chunk_scan_fwd(const mb200_ssd_params* p, void* stream) 
       !encode_map(&maps.x, p->x, L, p->headdim / 8, p->nheads, p->batch, p->x_seqlen_stride, p->x_head_stride,
                   p->x_batch_stride, kPT / 8))
     return MB200_ERR_CUDA;
-  cudaError_t e = cudaFuncSetAttribute(ssd_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSsdSmem);
+  const auto kern = p->seq_idx != nullptr ? ssd_fwd_kernel<true> : ssd_fwd_kernel<false>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSsdSmem);
   if (e != cudaSuccess) return MB200_ERR_CUDA;
-  ssd_fwd_kernel<<<(unsigned)ctas, kSsdThreads, kSsdSmem, static_cast<cudaStream_t>(stream)>>>(a, maps);
+  kern<<<(unsigned)ctas, kSsdThreads, kSsdSmem, static_cast<cudaStream_t>(stream)>>>(a, maps);
   if (cudaGetLastError() != cudaSuccess) return MB200_ERR_CUDA;
   note_launches(1);
   return MB200_OK;

@@ -102,6 +102,7 @@ class SsdParams(ctypes.Structure):
         ("B_batch_stride", _i64), ("B_seqlen_stride", _i64), ("B_group_stride", _i64),
         ("C_batch_stride", _i64), ("C_seqlen_stride", _i64), ("C_group_stride", _i64),
         ("dt_batch_stride", _i64), ("dt_seqlen_stride", _i64),
+        ("seq_idx", _vp), ("seq_idx_batch_stride", _i64), ("seq_idx_seqlen_stride", _i64),
         ("dt_min", ctypes.c_float), ("dt_max", ctypes.c_float),
         ("x_dtype", _i32), ("dt_softplus", _i32), ("D_per_dim", _i32), ("reserved", _i32),
     ]

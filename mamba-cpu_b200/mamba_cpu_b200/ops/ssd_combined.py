@@ -43,6 +43,7 @@ def _ssd_chunk_scan_fwd(
     z: Optional[torch.Tensor],
     dt_bias: Optional[torch.Tensor],
     initial_states: Optional[torch.Tensor],
+    seq_idx: Optional[torch.Tensor],
     dt_softplus: bool,
     dt_min: float,
     dt_max: float,
@@ -50,7 +51,8 @@ def _ssd_chunk_scan_fwd(
 ) -> Tuple[torch.Tensor, torch.Tensor]:
     """x, z (b, l, h, p) bf16 with 16-byte rows; dt (b, l, h) f32 (h contiguous); A, dt_bias (h)
     f32; B, C (b, l, g, n) bf16 with 16-byte rows; D (h) or (h, p) f32; initial_states (b, h, p, n)
-    f32. Returns out (b, l, h, p) and final_states (b, h, p, n) (empty unless want_final)."""
+    f32; seq_idx (b, l) int32 or None. Returns out (b, l, h, p) and final_states (b, h, p, n)
+    (empty unless want_final)."""
     b, l, h, p = x.shape
     g, n = B.shape[2], B.shape[3]
     out = torch.empty((b, l, h, p), dtype=x.dtype, device=x.device)
@@ -67,6 +69,9 @@ def _ssd_chunk_scan_fwd(
     prm.B_batch_stride, prm.B_seqlen_stride, prm.B_group_stride = B.stride(0), B.stride(1), B.stride(2)
     prm.C_batch_stride, prm.C_seqlen_stride, prm.C_group_stride = C.stride(0), C.stride(1), C.stride(2)
     prm.dt_batch_stride, prm.dt_seqlen_stride = dt.stride(0), dt.stride(1)
+    if seq_idx is not None:
+        prm.seq_idx = _lib.ptr(seq_idx)
+        prm.seq_idx_batch_stride, prm.seq_idx_seqlen_stride = seq_idx.stride(0), seq_idx.stride(1)
     prm.dt_min, prm.dt_max = float(dt_min), float(dt_max)
     prm.x_dtype = _lib.dtype_code(x.dtype)
     prm.dt_softplus = int(bool(dt_softplus))
@@ -78,7 +83,7 @@ def _ssd_chunk_scan_fwd(
 
 
 @_ssd_chunk_scan_fwd.register_fake
-def _(x, dt, A, B, C, D, z, dt_bias, initial_states, dt_softplus, dt_min, dt_max, want_final):
+def _(x, dt, A, B, C, D, z, dt_bias, initial_states, seq_idx, dt_softplus, dt_min, dt_max, want_final):
     b, l, h, p = x.shape
     n = B.shape[3]
     return (x.new_empty((b, l, h, p)),
@@ -125,14 +130,18 @@ def mamba_chunk_scan_combined(
     upstream does; the default (0, inf) only removes negative steps. ``chunk_size`` is checked
     and otherwise does not change the result beyond rounding: the kernel always works in chunks
     of 64 steps. This build takes bf16 x / z (B and C are used in bf16), dstate a multiple of 8
-    up to 128 and headdim a multiple of 32 up to 256. ``seq_idx``, ``cu_seqlens`` and
-    ``return_varlen_states`` (packed variable-length batches) are not supported, and neither is
-    the backward.
+    up to 128 and headdim a multiple of 32 up to 256.
+
+    ``seq_idx`` (batch, seqlen), non-decreasing along seqlen, packs several sequences into one
+    row: no step sees another sequence's steps and the state restarts from zero where the id
+    changes; ``initial_states`` belong to sequence 0 and ``final_states`` are the last
+    sequence's, as upstream. ``cu_seqlens`` / ``return_varlen_states`` (per-sequence final
+    states) are not supported, and neither is the backward.
     """
     if not x.is_cuda:
         raise ValueError("mamba_chunk_scan_combined (mamba_cpu_b200) expects CUDA tensors")
-    if seq_idx is not None or cu_seqlens is not None or return_varlen_states:
-        raise NotImplementedError("seq_idx / cu_seqlens / return_varlen_states are not supported")
+    if cu_seqlens is not None or return_varlen_states:
+        raise NotImplementedError("cu_seqlens / return_varlen_states are not supported")
     if not isinstance(chunk_size, int) or chunk_size <= 0:
         raise ValueError(f"chunk_size must be a positive int, got {chunk_size!r}")
     if x.dim() != 4:
@@ -154,6 +163,8 @@ def mamba_chunk_scan_combined(
         raise ValueError(f"z must have x's shape {tuple(x.shape)}, got {tuple(z.shape)}")
     if initial_states is not None and initial_states.shape != (b, h, p, n):
         raise ValueError(f"initial_states must be {(b, h, p, n)}, got {tuple(initial_states.shape)}")
+    if seq_idx is not None and tuple(seq_idx.shape) != (b, l):
+        raise ValueError(f"seq_idx must be {(b, l)}, got {tuple(seq_idx.shape)}")
     if x.dtype != torch.bfloat16:
         raise NotImplementedError(f"mamba_chunk_scan_combined: x dtype {x.dtype} (this build takes bfloat16)")
     if n % 8 != 0 or n > 128 or p % 32 != 0 or p > 256:
@@ -172,7 +183,8 @@ def mamba_chunk_scan_combined(
     D_k = None if D is None else D.to(f32).contiguous()
     bias_k = None if dt_bias is None else dt_bias.to(f32).contiguous()
     init_k = None if initial_states is None else initial_states.to(f32).contiguous()
-    out, final = _ssd_chunk_scan_fwd(x_k, dt_k, A_k, B_k, C_k, D_k, z_k, bias_k, init_k, bool(dt_softplus),
+    seq_k = None if seq_idx is None else seq_idx.to(torch.int32)
+    out, final = _ssd_chunk_scan_fwd(x_k, dt_k, A_k, B_k, C_k, D_k, z_k, bias_k, init_k, seq_k, bool(dt_softplus),
                                      dt_min, dt_max if not math.isnan(dt_max) else float("inf"),
                                      bool(return_final_states))
     return (out, final) if return_final_states else out

@@ -38,7 +38,7 @@ def _load():
         lib.oracle_state_update.restype = None
         lib.oracle_conv1d_update.argtypes = [_P] * 5 + [_I] * 5 + [ctypes.c_int]
         lib.oracle_conv1d_update.restype = None
-        lib.oracle_ssd_fwd.argtypes = [_P] * 11 + [_I] * 6 + [ctypes.c_int, ctypes.c_double, ctypes.c_double,
+        lib.oracle_ssd_fwd.argtypes = [_P] * 12 + [_I] * 6 + [ctypes.c_int, ctypes.c_double, ctypes.c_double,
                                                                 ctypes.c_int]
         lib.oracle_ssd_fwd.restype = ctypes.c_int
         lib.oracle_set_num_threads.argtypes = [ctypes.c_int]
@@ -181,17 +181,22 @@ def conv1d_update(x, conv_state, weight, bias=None, activation=None):
 
 
 def ssd_fwd(x, dt, A, B, C, D=None, z=None, dt_bias=None, initial_states=None, dt_softplus=False,
-            dt_limit=(0.0, float("inf"))):
+            dt_limit=(0.0, float("inf")), seq_idx=None):
     """Mamba-2 SSD scan, step by step in float64. x, z (b, l, h, p); dt (b, l, h); A, dt_bias (h);
-    B, C (b, l, g, n); D (h) or (h, p); initial_states (b, h, p, n). Returns (out, final_states)."""
+    B, C (b, l, g, n); D (h) or (h, p); initial_states (b, h, p, n); seq_idx (b, l) packed sequence
+    ids (the state restarts where the id changes). Returns (out, final_states)."""
     x, dt, A, B, C, D, z, dt_bias, init = map(_f32, (x, dt, A, B, C, D, z, dt_bias, initial_states))
+    if seq_idx is not None:
+        if hasattr(seq_idx, "detach"):
+            seq_idx = seq_idx.detach().cpu().numpy()
+        seq_idx = np.ascontiguousarray(np.asarray(seq_idx, dtype=np.int32))
     batch, seqlen, nheads, headdim = x.shape
     ngroups, dstate = B.shape[2], B.shape[3]
     out = np.empty(x.shape, np.float64)
     fin = np.empty((batch, nheads, headdim, dstate), np.float64)
     rc = _load().oracle_ssd_fwd(
-        _ptr(x), _ptr(dt), _ptr(A), _ptr(B), _ptr(C), _ptr(D), _ptr(z), _ptr(dt_bias), _ptr(init), _ptr(out),
-        _ptr(fin), batch, seqlen, nheads, headdim, ngroups, dstate, int(bool(dt_softplus)),
+        _ptr(x), _ptr(dt), _ptr(A), _ptr(B), _ptr(C), _ptr(D), _ptr(z), _ptr(dt_bias), _ptr(init), _ptr(seq_idx),
+        _ptr(out), _ptr(fin), batch, seqlen, nheads, headdim, ngroups, dstate, int(bool(dt_softplus)),
         float(dt_limit[0]), float(dt_limit[1]), int(D is not None and D.ndim == 2))
     if rc:
         raise ValueError(f"oracle_ssd_fwd rejected its arguments (status {rc})")

@@ -498,9 +498,13 @@ void oracle_conv1d_update(const float* x, double* conv_state, const float* w, co
  *   s[p][n] = exp(dt_t A[h]) s[p][n] + dt_t x[p] B[n];  y[p] = sum_n s[p][n] C[n] + D x[p];
  *   out = y * silu(z).
  * Layouts (dense): x, z, out (b, l, h, p); dt (b, l, h); B, C (b, l, g, n); D (h) or (h, p)
- * (D_per_dim); initial / final states (b, h, p, n). Head h reads group h / (h_total / g). */
+ * (D_per_dim); initial / final states (b, h, p, n); seq_idx (b, l) int32 or NULL. Head h reads
+ * group h / (h_total / g). With seq_idx (packed sequences) the state restarts from zero wherever
+ * the sequence id changes; the initial state belongs to sequence 0, as in upstream's
+ * _state_passing_fwd. */
 typedef struct {
   const float *x, *dt, *A, *B, *C, *D, *z, *dt_bias, *init;
+  const int32_t* seq_idx;
   double *out, *final_states;
   int64_t batch, seqlen, nheads, headdim, ngroups, dstate;
   int softplus, D_per_dim;
@@ -515,7 +519,14 @@ static void ssd_rows(int64_t lo, int64_t hi, void* vctx) {
     const int64_t b = r / H, h = r % H, g = h / (H / G);
     for (int64_t i = 0; i < P * N; ++i) s[i] = c->init ? (double)c->init[r * P * N + i] : 0.0;
     const double A = (double)c->A[h];
+    int32_t seq_prev = 0; /* the initial state belongs to sequence 0 */
     for (int64_t t = 0; t < L; ++t) {
+      if (c->seq_idx) { /* packed sequences: the state restarts where the sequence id changes */
+        const int32_t sq = c->seq_idx[b * L + t];
+        if (sq != seq_prev)
+          for (int64_t i = 0; i < P * N; ++i) s[i] = 0.0;
+        seq_prev = sq;
+      }
       double dt = (double)c->dt[(b * L + t) * H + h] + (c->dt_bias ? (double)c->dt_bias[h] : 0.0);
       if (c->softplus) dt = softplus_d(dt);
       dt = fmin(fmax(dt, c->dt_min), c->dt_max);
@@ -546,15 +557,15 @@ static void ssd_rows(int64_t lo, int64_t hi, void* vctx) {
 }
 
 int oracle_ssd_fwd(const float* x, const float* dt, const float* A, const float* B, const float* C,
-                   const float* D, const float* z, const float* dt_bias, const float* init, double* out,
-                   double* final_states, int64_t batch, int64_t seqlen, int64_t nheads, int64_t headdim,
-                   int64_t ngroups, int64_t dstate, int softplus, double dt_min, double dt_max,
-                   int D_per_dim) {
+                   const float* D, const float* z, const float* dt_bias, const float* init,
+                   const int32_t* seq_idx, double* out, double* final_states, int64_t batch, int64_t seqlen,
+                   int64_t nheads, int64_t headdim, int64_t ngroups, int64_t dstate, int softplus,
+                   double dt_min, double dt_max, int D_per_dim) {
   if (!x || !dt || !A || !B || !C || !out) return 1;
   if (batch < 0 || seqlen < 0 || nheads < 0 || headdim <= 0 || ngroups <= 0 || dstate <= 0) return 2;
   if (nheads % ngroups != 0) return 2;
-  ssd_ctx c = {x, dt, A, B, C, D, z, dt_bias, init, out, final_states, batch, seqlen, nheads, headdim,
-               ngroups, dstate, softplus, D_per_dim, dt_min, dt_max};
+  ssd_ctx c = {x, dt, A, B, C, D, z, dt_bias, init, seq_idx, out, final_states, batch, seqlen, nheads,
+               headdim, ngroups, dstate, softplus, D_per_dim, dt_min, dt_max};
   parallel_for(batch * nheads, ssd_rows, &c);
   return 0;
 }

@@ -127,3 +127,32 @@ def test_ssd_oracle_matches_reference(meta, a):
                            a.get("in_dt_bias"), dt_softplus=meta["dt_softplus"])
     assert_close(out, a["out"], 1e-4, 1e-5, "out", norm_tol=1e-5)
     assert_close(fin, a["final_states"], 1e-4, 1e-5, "final_states", norm_tol=1e-5)
+
+
+def test_ssd_oracle_packed_sequences_equal_separate_runs():
+    """seq_idx semantics of the float64 SSD oracle: a row packing several sequences gives, on each
+    sequence, exactly the oracle's run of that sequence alone (zero state at its start; the initial
+    state only for sequence 0), so the packed oracle inherits the pinning of the plain one."""
+    rng = np.random.default_rng(7)
+    b, l, h, p, g, n = 2, 50, 2, 4, 1, 8
+    x = rng.standard_normal((b, l, h, p)).astype(np.float32)
+    dt = (rng.standard_normal((b, l, h)) * 0.5).astype(np.float32)
+    A = -(1 + 15 * rng.random(h)).astype(np.float32)
+    B = rng.standard_normal((b, l, g, n)).astype(np.float32)
+    C = rng.standard_normal((b, l, g, n)).astype(np.float32)
+    z = rng.standard_normal((b, l, h, p)).astype(np.float32)
+    D = rng.standard_normal(h).astype(np.float32)
+    h0 = rng.standard_normal((b, h, p, n)).astype(np.float32)
+    bounds = [(0, 0, 13, 0), (0, 13, 14, 1), (0, 14, 50, 4), (1, 0, 30, 2), (1, 30, 50, 3)]  # (row, start, end, id)
+    seq = np.zeros((b, l), np.int32)
+    for r, s0, s1, sid in bounds:
+        seq[r, s0:s1] = sid
+    out, fin = f64.ssd_fwd(x, dt, A, B, C, D, z, None, h0, dt_softplus=True, seq_idx=seq)
+    for r, s0, s1, sid in bounds:
+        sl = slice(s0, s1)
+        init = h0[r:r + 1] if (s0 == 0 and sid == 0) else None
+        o1, f1 = f64.ssd_fwd(x[r:r + 1, sl], dt[r:r + 1, sl], A, B[r:r + 1, sl], C[r:r + 1, sl], D, z[r:r + 1, sl],
+                             None, init, dt_softplus=True)
+        np.testing.assert_allclose(out[r:r + 1, sl], o1, rtol=1e-12, atol=1e-12)
+        if s1 == l:
+            np.testing.assert_allclose(fin[r:r + 1], f1, rtol=1e-12, atol=1e-12)

@@ -80,14 +80,16 @@ def _inputs(b, l, h, p, g, n, seed=0, regime="mamba2", has_z=True, has_bias=True
     return dict(x=x, dt=dt, A=A, B=B, C=C, D=D, z=z, dt_bias=dt_bias, initial_states=h0)
 
 
-def _run_both(inp, dt_softplus=True, dt_limit=(0.0, float("inf"))):
+def _run_both(inp, dt_softplus=True, dt_limit=(0.0, float("inf")), seq_idx=None):
     dev = {k: (None if v is None else v.cuda()) for k, v in inp.items()}
     out, fin = mb.mamba_chunk_scan_combined(dev["x"], dev["dt"], dev["A"], dev["B"], dev["C"], 128, D=dev["D"],
                                             z=dev["z"], dt_bias=dev["dt_bias"], initial_states=dev["initial_states"],
+                                            seq_idx=None if seq_idx is None else seq_idx.cuda(),
                                             dt_softplus=dt_softplus, dt_limit=dt_limit, return_final_states=True)
     torch.cuda.synchronize()
     ref_out, ref_fin = f64.ssd_fwd(inp["x"], inp["dt"], inp["A"], inp["B"], inp["C"], inp["D"], inp["z"],
-                                   inp["dt_bias"], inp["initial_states"], dt_softplus=dt_softplus, dt_limit=dt_limit)
+                                   inp["dt_bias"], inp["initial_states"], dt_softplus=dt_softplus, dt_limit=dt_limit,
+                                   seq_idx=seq_idx)
     return out, fin, ref_out, ref_fin
 
 
@@ -131,6 +133,25 @@ def test_ssd_dt_limit_clamps_steps():
     _close(fin, rf, 5e-3, "final_states")
 
 
+@pytest.mark.parametrize("starts,first_id,init", [
+    ([0, 37, 64, 65, 200, 201, 330], 0, True),   # mid-chunk, at a chunk start, 1-step sequences
+    ([0, 128, 256], 0, False),                  # boundaries on chunk starts
+    ([0, 100], 3, True),                        # first id not 0: the initial state is dropped
+])
+def test_ssd_packed_sequences(starts, first_id, init):
+    """seq_idx: several sequences packed into each row; the oracle restarts the state at every id
+    change (tests/test_oracle_golden.py checks that against separate runs)."""
+    b, l = 2, 333
+    inp = _inputs(b, l, 2, 64, 1, 64, seed=21, regime="wide", init=init)
+    seq = torch.zeros(b, l, dtype=torch.int32)
+    for r in range(b):
+        for k, s0 in enumerate(starts):
+            seq[r, s0 + r:] = first_id + k  # row 1 shifted by one step
+    out, fin, ro, rf = _run_both(inp, seq_idx=seq)
+    _close(out, ro, 1e-2, "out")
+    _close(fin, rf, 5e-3, "final_states")
+
+
 def test_ssd_strided_views_from_one_projection():
     """x, z, B and C as slices of one (b, l, width) projection (the Mamba-2 in_proj split), read in
     place; dt as a strided slice too."""
@@ -169,7 +190,9 @@ def test_ssd_deterministic_and_errors():
     with pytest.raises(NotImplementedError):
         mb.mamba_chunk_scan_combined(dev["x"].float(), *args[1:])
     with pytest.raises(NotImplementedError):
-        mb.mamba_chunk_scan_combined(*args, seq_idx=torch.zeros(1, 200, dtype=torch.int32, device="cuda"))
+        mb.mamba_chunk_scan_combined(*args, cu_seqlens=torch.tensor([0, 200], dtype=torch.int32, device="cuda"))
+    with pytest.raises(ValueError):
+        mb.mamba_chunk_scan_combined(*args, seq_idx=torch.zeros(1, 199, dtype=torch.int32, device="cuda"))
     with pytest.raises(ValueError):
         mb.mamba_chunk_scan_combined(inp["x"], inp["dt"], inp["A"], inp["B"], inp["C"], 64)
     with pytest.raises(ValueError):
