@@ -54,6 +54,8 @@ extern "C" {
 
 /* Largest dstate the scan kernels accept (Mamba-1 uses 16). */
 #define MB200_MAX_DSTATE 16
+/* Largest dstate of the decode step (mb200_selective_state_update; Mamba-2 uses 64 / 128). */
+#define MB200_DECODE_MAX_DSTATE 256
 /* Timesteps between the states the forward saves for the backward (chunk_states). */
 #define MB200_CHUNK 64
 
@@ -273,7 +275,8 @@ MB200_API int mb200_causal_conv1d_bwd(const mb200_conv1d_params* p, const void* 
  * Mamba-1 layout; the multi-head layout is the same after flattening (heads*headdim -> dim):
  *   state (batch, dim, dstate) float32 or io_dtype (state_dtype); x, dt, z, out (batch, dim)
  *   io_dtype; A (dim, dstate) f32; B, C (batch, ngroups, dstate) bc_dtype contiguous;
- *   D, dt_bias (dim) f32 or NULL.
+ *   D, dt_bias (dim) f32 or NULL. dstate up to MB200_DECODE_MAX_DSTATE (the reference's PyTorch
+ *   version takes any dstate; Mamba-2 heads use 64 or 128).
  */
 typedef struct mb200_state_update_params {
   void* state;

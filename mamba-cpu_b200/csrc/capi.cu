@@ -498,7 +498,7 @@ MB200_API int mb200_selective_state_update(const mb200_state_update_params* p, v
   if (p == nullptr) return MB200_ERR_NULL_POINTER;
   if (p->batch < 0 || p->dim < 0 || p->dstate < 1 || p->ngroups < 1 || (p->dim % p->ngroups) != 0)
     return MB200_ERR_BAD_SHAPE;
-  if (p->dstate > MB200_MAX_DSTATE) return MB200_ERR_UNSUPPORTED;
+  if (p->dstate > MB200_DECODE_MAX_DSTATE) return MB200_ERR_UNSUPPORTED;
   if (!io_dtype_ok(p->io_dtype) || !bc_dtype_ok(p->io_dtype, p->bc_dtype) ||
       (p->state_dtype != MB200_F32 && p->state_dtype != p->io_dtype))
     return MB200_ERR_BAD_DTYPE;

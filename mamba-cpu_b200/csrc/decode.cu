@@ -2,8 +2,11 @@
 //
 // selective_state_update (mamba-cpu src/mamba_cpu/ops/selective_state_update.py:5-57):
 //   dt = softplus(dt + dt_bias); state = state * exp(dt * A) + dt * x * B; out = <state, C> + D x,
-//   out *= silu(z). One thread per (batch, channel); the dstate entries of its state row live in
-//   registers. B / C rows are shared by the channels of a group and read through L1.
+//   out *= silu(z). dstate <= 16 (Mamba-1): one thread per (batch, channel), the dstate entries of
+//   its state row in registers. Wider states (Mamba-2's 64 / 128 per head channel): one warp per
+//   (batch, channel), lane l owning entries l, l + 32, ..., so the state row, A row and B / C rows
+//   move as coalesced 128-byte lines; <state, C> is summed over the warp by shuffles. B / C rows
+//   are shared by the channels of a group and read through L1.
 // causal_conv1d_update (src/mamba_cpu/ops/causal_conv1d.py:56-85): the conv state window is
 //   shifted by seqlen new inputs in place and every new input yields one output.
 #include "decode.cuh"
@@ -44,6 +47,44 @@ __global__ void state_update_kernel(const mb200_state_update_params p) {
   static_cast<TI*>(p.out)[i] = from_f32<TI>(y);
 }
 
+constexpr int kWideWarps = 8;  // rows (warps) per CTA of the wide-state kernel
+
+template <typename TI, typename TW, typename TS>
+__global__ void __launch_bounds__(32 * kWideWarps) state_update_wide_kernel(const mb200_state_update_params p) {
+  const int lane = threadIdx.x & 31;
+  const int64_t i = (int64_t)blockIdx.x * kWideWarps + (threadIdx.x >> 5);
+  if (i >= p.batch * p.dim) return;  // warp-uniform
+  const int64_t b = i / p.dim, d = i % p.dim;
+  const int64_t g = d / (p.dim / p.ngroups);
+  const int N = (int)p.dstate;
+  TS* st = static_cast<TS*>(p.state) + i * N;
+  const TW* Bp = static_cast<const TW*>(p.B) + (b * p.ngroups + g) * N;
+  const TW* Cp = static_cast<const TW*>(p.C) + (b * p.ngroups + g) * N;
+  const float* Ap = p.A + d * N;
+  const float x = to_f32<TI>(static_cast<const TI*>(p.x)[i]);
+  float dt = to_f32<TI>(static_cast<const TI*>(p.dt)[i]) + (p.dt_bias ? p.dt_bias[d] : 0.f);
+  if (p.dt_softplus) dt = softplus_f(dt);
+  const float dtx = dt * x;
+  const float dtl = dt * kLog2e;
+  float y = 0.f;
+  for (int n = lane; n < N; n += 32) {
+    const float a = ex2(dtl * Ap[n]);
+    const float s = fmaf(to_f32<TS>(st[n]), a, dtx * to_f32<TW>(__ldg(Bp + n)));
+    st[n] = from_f32<TS>(s);
+    y = fmaf(s, to_f32<TW>(__ldg(Cp + n)), y);
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) y += __shfl_xor_sync(0xffffffffu, y, off);
+  if (lane == 0) {
+    if (p.D) y = fmaf(x, p.D[d], y);
+    if (p.z) {
+      const float z = to_f32<TI>(static_cast<const TI*>(p.z)[i]);
+      y *= z * sigmoid_f(z);
+    }
+    static_cast<TI*>(p.out)[i] = from_f32<TI>(y);
+  }
+}
+
 template <typename T>
 __global__ void conv_update_kernel(const mb200_conv1d_update_params p) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -76,6 +117,14 @@ __global__ void conv_update_kernel(const mb200_conv1d_update_params p) {
 template <typename TI, typename TW>
 cudaError_t su_state(const mb200_state_update_params& p, cudaStream_t stream) {
   const int64_t n = p.batch * p.dim;
+  if (p.dstate > kMaxState) {
+    const unsigned wblocks = (unsigned)((n + kWideWarps - 1) / kWideWarps);
+    if (p.state_dtype == MB200_F32)
+      state_update_wide_kernel<TI, TW, float><<<wblocks, 32 * kWideWarps, 0, stream>>>(p);
+    else
+      state_update_wide_kernel<TI, TW, TI><<<wblocks, 32 * kWideWarps, 0, stream>>>(p);
+    return cudaGetLastError();
+  }
   const unsigned blocks = (unsigned)((n + 127) / 128);
   if (p.state_dtype == MB200_F32)
     state_update_kernel<TI, TW, float><<<blocks, 128, 0, stream>>>(p);

@@ -19,6 +19,7 @@ LIB_PATH = os.environ.get("MAMBA_B200_LIB", os.path.join(_HERE, "_lib", "libmamb
 
 F32, BF16, F16 = 0, 1, 2
 MAX_DSTATE = 16
+DECODE_MAX_DSTATE = 256
 CHUNK = 64
 CONV_MAX_WIDTH = 8
 

@@ -1,5 +1,9 @@
 """Hugging Face route: run transformers' Mamba-family mixers on the B200 kernels.
 
+Mamba-2 models (an addition: the reference patches the Mamba-1 families only) are routed the same
+way through ``mamba_chunk_scan_combined`` and a composed ``mamba_split_conv1d_scan_combined``,
+for inference.
+
 mamba-cpu's ``hf.patch_transformers`` (src/mamba_cpu/hf.py:63-102) wraps module-level functions
 (``mamba_selective_scan``, ...) that transformers 5.x no longer has. In transformers 5.5 each
 mixer resolves its fast path when it is constructed: ``MambaMixer.__init__`` calls
@@ -25,12 +29,27 @@ from typing import Optional
 import torch
 import torch.nn.functional as F
 
-from .ops import causal_conv1d_fn, causal_conv1d_update, selective_scan_fn, selective_state_update
+from .ops import (
+    causal_conv1d_fn,
+    causal_conv1d_update,
+    mamba_chunk_scan_combined,
+    selective_scan_fn,
+    selective_state_update,
+)
 
 _KEYS = ("causal-conv1d", "mamba-ssm", "falcon_mamba-ssm")
-_MODELS = ("mamba", "falcon_mamba", "jamba")
-_GLOBALS = ("causal_conv1d_fn", "causal_conv1d_update", "selective_state_update", "selective_scan_fn",
-            "mamba_inner_fn", "falcon_mamba_inner_fn")
+_MODELS = ("mamba", "falcon_mamba", "jamba", "mamba2")
+# the module globals each modeling module's fast path reads
+_MODEL_GLOBALS = {
+    "mamba": ("causal_conv1d_fn", "causal_conv1d_update", "selective_state_update", "selective_scan_fn",
+              "mamba_inner_fn"),
+    "falcon_mamba": ("causal_conv1d_fn", "causal_conv1d_update", "selective_state_update", "selective_scan_fn",
+                     "falcon_mamba_inner_fn"),
+    "jamba": ("causal_conv1d_fn", "causal_conv1d_update", "selective_state_update", "selective_scan_fn",
+              "mamba_inner_fn"),
+    "mamba2": ("causal_conv1d_fn", "causal_conv1d_update", "selective_state_update", "mamba_chunk_scan_combined",
+               "mamba_split_conv1d_scan_combined"),
+}
 _saved: Optional[dict] = None
 
 
@@ -89,6 +108,66 @@ def mamba_inner_fn(xz, conv1d_weight, conv1d_bias, x_proj_weight, delta_proj_wei
     return F.linear(y.transpose(1, 2), out_proj_weight, out_proj_bias)
 
 
+def ssd_chunk_scan(x, dt, A, B, C, chunk_size, D=None, z=None, dt_bias=None, initial_states=None, seq_idx=None,
+                   cu_seqlens=None, dt_softplus=False, dt_limit=(0.0, float("inf")), return_final_states=False,
+                   return_varlen_states=False):
+    """``mamba_chunk_scan_combined`` for transformers' Mamba-2 mixer. The SSD kernel multiplies in
+    bf16: x, z, B and C of another dtype (an fp32 model) are rounded to bf16 and the output is
+    returned in x's dtype (upstream's Triton kernels likewise multiply fp32 inputs in tf32)."""
+    dtype = x.dtype
+
+    def bf(t):
+        return None if t is None else (t if t.dtype == torch.bfloat16 else t.to(torch.bfloat16))
+
+    r = mamba_chunk_scan_combined(bf(x), dt, A, bf(B), bf(C), chunk_size, D=D, z=bf(z), dt_bias=dt_bias,
+                                  initial_states=initial_states, seq_idx=seq_idx, cu_seqlens=cu_seqlens,
+                                  dt_softplus=dt_softplus, dt_limit=dt_limit, return_final_states=return_final_states,
+                                  return_varlen_states=return_varlen_states)
+    if return_final_states:
+        return r[0].to(dtype), r[1]
+    return r.to(dtype)
+
+
+def mamba_split_conv1d_scan_combined(zxbcdt, conv1d_weight, conv1d_bias, dt_bias, A, D, chunk_size,
+                                     initial_states=None, seq_idx=None, dt_limit=(0.0, float("inf")),
+                                     return_final_states=False, activation="silu", rmsnorm_weight=None,
+                                     rmsnorm_eps=1e-6, outproj_weight=None, outproj_bias=None, headdim=None,
+                                     ngroups=1, norm_before_gate=True):
+    """The Mamba-2 mixer body (mamba_ssm's ``mamba_split_conv1d_scan_combined`` signature) on this
+    package's ops: split ``zxbcdt`` (batch, seqlen, [z | x B C | dt]), causal conv1d with SiLU over
+    x B C, the SSD scan, the gated RMS norm (over the whole inner dimension, as transformers'
+    ``MambaRMSNormGated``) and the output projection. Forward only: the SSD backward is not built,
+    so gradients through it raise ``NotImplementedError``."""
+    if D is None or headdim is None:
+        raise ValueError("mamba_split_conv1d_scan_combined needs D and headdim")
+    nheads = A.shape[0]
+    dim = nheads * headdim
+    batch, seqlen, _ = zxbcdt.shape
+    dstate = (zxbcdt.shape[-1] - 2 * dim - nheads) // (2 * ngroups)
+    z, xbc, dt = torch.split(zxbcdt, [dim, dim + 2 * ngroups * dstate, nheads], dim=-1)
+    xbc = causal_conv1d_fn(xbc.transpose(1, 2), conv1d_weight, conv1d_bias,
+                           activation=activation if activation in ("silu", "swish") else None).transpose(1, 2)
+    x, B, C = torch.split(xbc, [dim, ngroups * dstate, ngroups * dstate], dim=-1)
+    r = ssd_chunk_scan(x.reshape(batch, seqlen, nheads, headdim), dt, A, B.reshape(batch, seqlen, ngroups, dstate),
+                       C.reshape(batch, seqlen, ngroups, dstate), chunk_size, D=D,
+                       z=None if rmsnorm_weight is not None else z.reshape(batch, seqlen, nheads, headdim),
+                       dt_bias=dt_bias, initial_states=initial_states, seq_idx=seq_idx, dt_softplus=True,
+                       dt_limit=dt_limit, return_final_states=return_final_states)
+    y, last = (r[0], r[1]) if return_final_states else (r, None)
+    y = y.reshape(batch, seqlen, dim)
+    if rmsnorm_weight is not None:
+        ct = torch.promote_types(y.dtype, torch.float32)
+        yf = y.to(ct)
+        if not norm_before_gate:
+            yf = yf * F.silu(z.to(ct))
+        yf = yf * torch.rsqrt(yf.pow(2).mean(-1, keepdim=True) + rmsnorm_eps) * rmsnorm_weight.to(ct)
+        if norm_before_gate:
+            yf = yf * F.silu(z.to(ct))
+        y = yf.to(y.dtype)
+    out = F.linear(y, outproj_weight, outproj_bias) if outproj_weight is not None else y
+    return (out, last) if return_final_states else out
+
+
 def _values() -> dict:
     return {
         "causal_conv1d_fn": causal_conv1d_fn,
@@ -97,6 +176,8 @@ def _values() -> dict:
         "selective_scan_fn": selective_scan_fn,
         "mamba_inner_fn": mamba_inner_fn,
         "falcon_mamba_inner_fn": mamba_inner_fn,
+        "mamba_chunk_scan_combined": ssd_chunk_scan,
+        "mamba_split_conv1d_scan_combined": mamba_split_conv1d_scan_combined,
     }
 
 
@@ -107,13 +188,17 @@ def kernel_modules() -> dict:
     conv.causal_conv1d_fn = v["causal_conv1d_fn"]
     conv.causal_conv1d_update = v["causal_conv1d_update"]
     ssm = types.ModuleType("mamba_cpu_b200.hf.mamba_ssm")
-    for name in ("selective_scan_fn", "selective_state_update", "mamba_inner_fn", "falcon_mamba_inner_fn"):
+    for name in ("selective_scan_fn", "selective_state_update", "mamba_inner_fn", "falcon_mamba_inner_fn",
+                 "mamba_chunk_scan_combined", "mamba_split_conv1d_scan_combined"):
         setattr(ssm, name, v[name])
     return {"causal-conv1d": conv, "mamba-ssm": ssm, "falcon_mamba-ssm": ssm}
 
 
 def patch_transformers() -> list:
-    """Route transformers' Mamba / FalconMamba / Jamba mixers with CUDA weights to this package.
+    """Route transformers' Mamba / FalconMamba / Jamba / Mamba-2 mixers with CUDA weights to this package.
+
+    Mamba-2 (``Mamba2ForCausalLM``) runs its prefill on the SSD chunk scan and its cached decoding on
+    the conv / state-update kernels; it is inference only (the SSD backward is not built).
 
     Call before building the model (mixers resolve their kernels in ``__init__``); modeling
     modules already imported also get their globals set, so earlier mixers switch too. Returns
@@ -134,17 +219,13 @@ def patch_transformers() -> list:
             mod = importlib.import_module(f"transformers.models.{model}.modeling_{model}")
         except ImportError:
             continue
-        for name in _GLOBALS:
-            if name == "falcon_mamba_inner_fn" and model != "falcon_mamba":
-                continue
-            if name == "mamba_inner_fn" and model == "falcon_mamba":
-                continue
+        for name in _MODEL_GLOBALS[model]:
             _saved["globals"].setdefault((mod.__name__, name), getattr(mod, name, _MISSING))
             setattr(mod, name, values[name])
-        if model == "jamba":
-            # JambaMambaMixer.__init__ caches the availability in a module global that its forward
-            # reads (transformers/models/jamba/modeling_jamba.py); mixers built before patching
-            # would otherwise turn config.use_mamba_kernels off on their first CUDA forward.
+        if model in ("jamba", "mamba2"):
+            # JambaMambaMixer.__init__ / Mamba2Mixer.__init__ cache the availability in a module
+            # global that their forward reads (transformers/models/{jamba,mamba2}/modeling_*.py);
+            # mixers built before patching would otherwise keep the sequential path.
             _saved["globals"].setdefault((mod.__name__, "is_fast_path_available"),
                                          getattr(mod, "is_fast_path_available", _MISSING))
             mod.is_fast_path_available = True
@@ -167,7 +248,10 @@ def unpatch_transformers() -> None:
             mapping[k] = v
     for (modname, name), v in _saved["globals"].items():
         mod = importlib.import_module(modname)
-        if v is _MISSING:
+        if v is _MISSING and name == "is_fast_path_available":
+            # mixers built while patched read this global in forward: leave them the sequential path
+            setattr(mod, name, False)
+        elif v is _MISSING:
             if hasattr(mod, name):
                 delattr(mod, name)
         else:

@@ -78,8 +78,8 @@ def selective_state_update(
         raise ValueError(f"mamba_cpu_b200 runs on CUDA tensors, got device {x.device}")
     has_heads = state.dim() > 3
     batch, dstate = state.shape[0], state.shape[-1]
-    if dstate > _lib.MAX_DSTATE:
-        raise NotImplementedError(f"dstate > {_lib.MAX_DSTATE} is not supported by the B200 kernels")
+    if dstate > _lib.DECODE_MAX_DSTATE:
+        raise NotImplementedError(f"dstate > {_lib.DECODE_MAX_DSTATE} is not supported by the B200 kernels")
     lead = tuple(state.shape[1:-1])
     dim = 1
     for s in lead:

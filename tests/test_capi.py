@@ -124,7 +124,7 @@ def test_conv_and_decode_validation():
     assert _lib.lib.mb200_causal_conv1d_update(u, None) == 2  # state_len < width - 1
     s = _lib.StateUpdateParams()
     s.state = s.x = s.dt = s.A = s.B = s.C = s.out = 0x1000
-    s.batch, s.dim, s.dstate, s.ngroups = 1, 4, 32, 1
+    s.batch, s.dim, s.dstate, s.ngroups = 1, 4, _lib.DECODE_MAX_DSTATE + 1, 1  # beyond the decode limit
     assert _lib.lib.mb200_selective_state_update(s, None) == 5
 
 
