@@ -201,3 +201,13 @@ def test_ssd_deterministic_and_errors():
     out = mb.mamba_chunk_scan_combined(x, *args[1:])
     with pytest.raises(NotImplementedError):
         out.float().sum().backward()
+
+
+@pytest.mark.slow
+def test_ssd_long_sequence_slice():
+    """seqlen 65536 (1,024 chunks of carried state) on two heads of the 2.7B layer shape (headdim 64,
+    dstate 128), in the Mamba-2 initialisation regime (long memory), against float64."""
+    inp = _inputs(1, 65536, 2, 64, 1, 128, seed=31, regime="mamba2", dmode="h", init=True)
+    out, fin, ro, rf = _run_both(inp)
+    _close(out, ro, 1e-2, "out")
+    _close(fin, rf, 5e-3, "final_states")
