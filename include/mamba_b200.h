@@ -326,11 +326,11 @@ MB200_API int mb200_causal_conv1d_update(const mb200_conv1d_update_params* p, vo
  * which is the Mamba-1 selective scan with channels = nheads * headdim, A broadcast over dstate
  * and delta broadcast over headdim (the reference's selective_scan_fwd_f32 on those inputs,
  * csrc/selective_scan.cpp:120-145, computes the same values).
- *   x, z, out       : (batch, seqlen, nheads, headdim) bf16; headdim contiguous, other strides
+ *   x, z, out       : (batch, seqlen, nheads, headdim) x_dtype; headdim contiguous, other strides
  *                     below (out dense). Row starts (x, z, out, B, C) 16-byte aligned.
  *   dt              : (batch, seqlen, nheads) float32, nheads contiguous, strides below
  *   A               : (nheads) float32; dt_bias (nheads) float32 or NULL
- *   B, C            : (batch, seqlen, ngroups, dstate) bf16, dstate contiguous; head h reads
+ *   B, C            : (batch, seqlen, ngroups, dstate) x_dtype, dstate contiguous; head h reads
  *                     group h / (nheads / ngroups)
  *   D               : (nheads) or (nheads, headdim) (D_per_dim = 1) float32, or NULL
  *   initial_states  : (batch, nheads, headdim, dstate) float32 or NULL (zeros)
@@ -341,8 +341,9 @@ MB200_API int mb200_causal_conv1d_update(const mb200_conv1d_update_params* p, vo
  *                     from zero where the index changes. initial_states belong to sequence 0 (as
  *                     upstream: they are dropped if seq_idx[b, 0] != 0), final_states are the
  *                     last sequence's.
- * Limits of this build: x_dtype MB200_BF16, dstate a multiple of 8 up to 128, headdim a multiple
- * of 32 up to 256 (MB200_ERR_UNSUPPORTED otherwise). One kernel launch, no scratch memory.
+ * Limits of this build: x_dtype MB200_BF16 or MB200_F16 (x, z, B, C and out all of that type),
+ * dstate a multiple of 8 up to 128, headdim a multiple of 32 up to 256 (MB200_ERR_UNSUPPORTED
+ * otherwise). One kernel launch, no scratch memory.
  */
 typedef struct mb200_ssd_params {
   const void* x;

@@ -13,13 +13,15 @@
 // batch x nheads x headdim / 32. A CTA is small (128 threads, ~53 KB of shared memory, 128 TMEM
 // columns) so that four fit on an SM and a whole Mamba-2 layer's grid is resident at once.
 //
-// Tensor cores: every product is one tcgen05.mma (kind::f16, bf16 operands, float32 accumulators
+// Tensor cores: every product is one tcgen05.mma (kind::f16, bf16 or fp16 operands -- the input's
+// 16-bit type --, float32 accumulators
 // in Tensor Memory) issued by one thread, operands in shared memory in the no-swizzle core-matrix
 // layout (8 rows x 16 bytes per 128-byte core matrix), completion signalled on an mbarrier by
 // tcgen05.commit. G, C S^T and M X have M = 64 (row m of the accumulator in TMEM lane
 // (m % 16) + 32 (m / 16), i.e. lanes 0-15 of each warp's quarter); X'^T B has M = 128 (row n in
-// lane n). The bf16 copy of S that feeds C S^T is split in two (S = hi + lo, both bf16), so the
-// carried state enters the product with ~16 significant bits; M and X' are rounded to bf16 once.
+// lane n). The 16-bit copy of S that feeds C S^T is split in two (S = hi + lo), so the carried
+// state enters the product with about twice the 16-bit type's precision; M and X' are rounded to
+// the 16-bit type once.
 //
 // Shared memory (PT = 32 headdim columns per CTA). Every tile is stored as [column piece c8][row
 // r][8 elements]: 16 bytes per (row, 8 columns), so core matrix (r / 8, c8) -- 8 rows x 16 bytes
@@ -31,7 +33,7 @@
 //                        first 8 pieces
 //   sB   [16][64 t]      B tile; K-major operand of C B^T, MN-major operand of X'^T B
 //   sX   [PT/8][64 t]    X tile (MN-major operand of M X)
-//   sSh, sSl [PT/8][128 n]  bf16 hi / lo parts of S (MN-major operand of C S^T); X' [PT/8][64 t]
+//   sSh, sSl [PT/8][128 n]  16-bit hi / lo parts of S (MN-major operand of C S^T); X' [PT/8][64 t]
 //                        reuses sSl once C S^T is done
 // dstate is zero-padded to 128 (the padded columns of B stay zero, so S's padded rows stay zero).
 // TMEM (128 columns): [0, 64) G, then M X in [0, PT); [64, 64 + PT) C S^T; [96, 128) X'^T B.
@@ -69,16 +71,16 @@ constexpr int kOffBar = kOffF + kFloats * 4;
 constexpr int kSsdSmem = kOffBar + 32;
 
 struct SsdArgs {
-  const __nv_bfloat16* x;
+  const uint16_t* x;  // bf16 or fp16 bits (the F16 template argument)
   const float* dt;
   const float* A;
-  const __nv_bfloat16* B;
-  const __nv_bfloat16* C;
+  const uint16_t* B;
+  const uint16_t* C;
   const float* D;
-  const __nv_bfloat16* z;
+  const uint16_t* z;
   const float* dt_bias;
   const float* init;
-  __nv_bfloat16* out;
+  uint16_t* out;
   float* final_states;
   int64_t L, H, P, G, N;
   int64_t xbs, xls, xhs, zbs, zls, zhs, Bbs, Bls, Bgs, Cbs, Cls, Cgs, dtbs, dtls;
@@ -100,14 +102,14 @@ __device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t
          ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
 }
 
-// Instruction descriptor of kind::f16: bf16 A and B, float32 accumulator, M x N, operand majors
-// (0 = K-major, 1 = MN-major).
-constexpr uint32_t idesc_bf16(int M, int N, int a_mn, int b_mn) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) |
-         ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+// Instruction descriptor of kind::f16: A and B both bf16 (format 1) or both fp16 (format 0), float32
+// accumulator, M x N, operand majors (0 = K-major, 1 = MN-major).
+constexpr uint32_t idesc_16(int M, int N, int a_mn, int b_mn, bool f16) {
+  return (1u << 4) | ((f16 ? 0u : 1u) << 7) | ((f16 ? 0u : 1u) << 10) | ((uint32_t)a_mn << 15) |
+         ((uint32_t)b_mn << 16) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
-__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+__device__ __forceinline__ void umma_16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
   asm volatile(
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
@@ -121,12 +123,23 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
                : "memory");
 }
 
-__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
-  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
-  return *reinterpret_cast<const uint32_t*>(&v);
+// Two floats to / from a pair of 16-bit values (bf16, or fp16 when F16).
+template <bool F16>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  if constexpr (F16) {
+    const __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&v);
+  } else {
+    const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&v);
+  }
 }
-__device__ __forceinline__ float2 unpack_bf16(uint32_t w) {
-  return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w));
+template <bool F16>
+__device__ __forceinline__ float2 unpack2(uint32_t w) {
+  if constexpr (F16)
+    return __half22float2(*reinterpret_cast<const __half2*>(&w));
+  else
+    return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w));
 }
 
 // Wait for the mbarrier phase with the given parity (tensor-core or copy completion): try_wait
@@ -172,8 +185,9 @@ struct SsdMaps {
 // Thread roles (128 threads, 4 warps): S row n = tid (TMEM lane n of X'^T B). The 64-row
 // accumulators live in lanes 0-15 of each warp's quarter, so lane l < 16 of warp w owns chunk row
 // i = 16 w + l (masked decay matrix, outputs) and lane l >= 16 owns row 16 w + l - 16 of X'.
-// SEQ: packed sequences (seq_idx); the other instantiation drops the sequence masks.
-template <bool SEQ>
+// SEQ: packed sequences (seq_idx); the other instantiation drops the sequence masks. F16: fp16
+// x / z / B / C (and fp16 operands of every product) instead of bf16.
+template <bool SEQ, bool F16>
 __global__ void __launch_bounds__(kSsdThreads, 4) ssd_fwd_kernel(SsdArgs a, const __grid_constant__ SsdMaps maps) {
   extern __shared__ __align__(1024) uint8_t smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -237,7 +251,7 @@ __global__ void __launch_bounds__(kSsdThreads, 4) ssd_fwd_kernel(SsdArgs a, cons
     S[p] = (a.init != nullptr && tid < N) ? a.init[((b * a.H + h) * a.P + p0 + p) * a.N + tid] : 0.f;
   const float A2 = a.A[h] * kLog2e;
   const float bias = a.dt_bias != nullptr ? a.dt_bias[h] : 0.f;
-  const __nv_bfloat16* zbase = a.z != nullptr ? a.z + b * a.zbs + h * a.zhs + p0 : nullptr;
+  const uint16_t* zbase = a.z != nullptr ? a.z + b * a.zbs + h * a.zhs + p0 : nullptr;
   const float* dtbase = a.dt + b * a.dtbs + h;
 
   tmem_fence_before_sync();
@@ -246,9 +260,9 @@ __global__ void __launch_bounds__(kSsdThreads, 4) ssd_fwd_kernel(SsdArgs a, cons
   const uint32_t tbase = *tslot;
   const uint32_t trow = tbase + ((uint32_t)(warp * 32) << 16);  // this warp's lanes
 
-  constexpr uint32_t kIdG = idesc_bf16(kQ, kQ, 0, 0);
-  constexpr uint32_t kIdY = idesc_bf16(kQ, kPT, 0, 1);
-  constexpr uint32_t kIdS = idesc_bf16(kNP, kPT, 1, 1);
+  constexpr uint32_t kIdG = idesc_16(kQ, kQ, 0, 0, F16);
+  constexpr uint32_t kIdY = idesc_16(kQ, kPT, 0, 1, F16);
+  constexpr uint32_t kIdS = idesc_16(kNP, kPT, 1, 1, F16);
   // Column-piece-major tiles: core matrices 128 bytes apart along the rows, rows * 16 bytes
   // apart along the column pieces. K-major (rows = M / N): LBO = piece stride, SBO = 128;
   // MN-major (rows = K): LBO = 128, SBO = piece stride. A K step of 16 is two pieces (K-major)
@@ -268,7 +282,7 @@ __global__ void __launch_bounds__(kSsdThreads, 4) ssd_fwd_kernel(SsdArgs a, cons
     const int64_t t0 = k * kQ;
     const int valid = (int)(a.L - t0 < kQ ? a.L - t0 : kQ);
 
-    // ---- S_prev as bf16 hi + lo (row n = tid), this chunk's z (registers), dt and its sums
+    // ---- S_prev as 16-bit hi + lo (row n = tid), this chunk's z (registers), dt and its sums
     uint4 zv[kPT / 8];
     if (lo16 && zbase != nullptr && crow < valid) {
 #pragma unroll
@@ -280,9 +294,9 @@ __global__ void __launch_bounds__(kSsdThreads, 4) ssd_fwd_kernel(SsdArgs a, cons
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         const float v0 = S[c * 8 + 2 * q], v1 = S[c * 8 + 2 * q + 1];
-        hi[q] = pack_bf16(v0, v1);
-        const float2 hv = unpack_bf16(hi[q]);
-        lo[q] = pack_bf16(v0 - hv.x, v1 - hv.y);
+        hi[q] = pack2<F16>(v0, v1);
+        const float2 hv = unpack2<F16>(hi[q]);
+        lo[q] = pack2<F16>(v0 - hv.x, v1 - hv.y);
       }
       const uint32_t off = core16(tid, c, kNP);
       *reinterpret_cast<uint4*>(smem + kOffSh + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
@@ -324,13 +338,13 @@ __global__ void __launch_bounds__(kSsdThreads, 4) ssd_fwd_kernel(SsdArgs a, cons
     if (tid == 0) {
       tmem_fence_after_sync();
       for (int s = 0; s < ksteps; ++s)
-        umma_bf16(tbase, sdesc(sCM + s * 2 * kPiece, kPiece, 128), sdesc(sB + s * 2 * kPiece, kPiece, 128), kIdG,
+        umma_16(tbase, sdesc(sCM + s * 2 * kPiece, kPiece, 128), sdesc(sB + s * 2 * kPiece, kPiece, 128), kIdG,
                   s > 0);
       for (int s = 0; s < ksteps; ++s)
-        umma_bf16(tbase + kColYo, sdesc(sCM + s * 2 * kPiece, kPiece, 128), sdesc(sSh + s * 256, 128, kPieceS), kIdY,
+        umma_16(tbase + kColYo, sdesc(sCM + s * 2 * kPiece, kPiece, 128), sdesc(sSh + s * 256, 128, kPieceS), kIdY,
                   s > 0);
       for (int s = 0; s < ksteps; ++s)
-        umma_bf16(tbase + kColYo, sdesc(sCM + s * 2 * kPiece, kPiece, 128), sdesc(sSl + s * 256, 128, kPieceS), kIdY,
+        umma_16(tbase + kColYo, sdesc(sCM + s * 2 * kPiece, kPiece, 128), sdesc(sSl + s * 256, 128, kPieceS), kIdY,
                   1);
       umma_commit(bar);
     }
@@ -360,8 +374,8 @@ __global__ void __launch_bounds__(kSsdThreads, 4) ssd_fwd_kernel(SsdArgs a, cons
             const float m1 = (j + 1 <= i && sj.y == seq_i) ? gv[jj + 1] * ex2(cs - cj.y) * dj.y : 0.f;
             const float m2 = (j + 2 <= i && sj.z == seq_i) ? gv[jj + 2] * ex2(cs - cj.z) * dj.z : 0.f;
             const float m3 = (j + 3 <= i && sj.w == seq_i) ? gv[jj + 3] * ex2(cs - cj.w) * dj.w : 0.f;
-            pk[jj / 2] = pack_bf16(m0, m1);
-            pk[jj / 2 + 1] = pack_bf16(m2, m3);
+            pk[jj / 2] = pack2<F16>(m0, m1);
+            pk[jj / 2 + 1] = pack2<F16>(m2, m3);
           }
           w0 = make_uint4(pk[0], pk[1], pk[2], pk[3]);
           w1 = make_uint4(pk[4], pk[5], pk[6], pk[7]);
@@ -382,8 +396,8 @@ __global__ void __launch_bounds__(kSsdThreads, 4) ssd_fwd_kernel(SsdArgs a, cons
           uint32_t o[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const float2 f = unpack_bf16(in[e]);
-            o[e] = pack_bf16(f.x * wx, f.y * wx);
+            const float2 f = unpack2<F16>(in[e]);
+            o[e] = pack2<F16>(f.x * wx, f.y * wx);
           }
           *reinterpret_cast<uint4*>(smem + kOffXs + off) = make_uint4(o[0], o[1], o[2], o[3]);
         }
@@ -397,9 +411,9 @@ __global__ void __launch_bounds__(kSsdThreads, 4) ssd_fwd_kernel(SsdArgs a, cons
     if (tid == 0) {
       tmem_fence_after_sync();
       for (int s = 0; s < kQ / 16; ++s)
-        umma_bf16(tbase, sdesc(sCM + s * 2 * kPiece, kPiece, 128), sdesc(sX + s * 256, 128, kPiece), kIdY, s > 0);
+        umma_16(tbase, sdesc(sCM + s * 2 * kPiece, kPiece, 128), sdesc(sX + s * 256, 128, kPiece), kIdY, s > 0);
       for (int s = 0; s < kQ / 16; ++s)
-        umma_bf16(tbase + kColSl, sdesc(sB + s * 256, 128, kPiece), sdesc(sXs + s * 256, 128, kPiece), kIdS, s > 0);
+        umma_16(tbase + kColSl, sdesc(sB + s * 256, 128, kPiece), sdesc(sXs + s * 256, 128, kPiece), kIdS, s > 0);
       umma_commit(bar);
     }
     mbar_wait_spin(bar, phase);
@@ -423,7 +437,7 @@ __global__ void __launch_bounds__(kSsdThreads, 4) ssd_fwd_kernel(SsdArgs a, cons
       if (lo16 && crow < valid) {
         const float eo = seq_i == seq_prev ? ex2(cs) : 0.f;  // the carried state, if it is this row's sequence
         const int64_t t = t0 + crow;
-        __nv_bfloat16* orow = a.out + ((b * a.L + t) * a.H + h) * a.P + p0 + 16 * hf;
+        uint16_t* orow = a.out + ((b * a.L + t) * a.H + h) * a.P + p0 + 16 * hf;
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
           const uint4 xq = xv[2 * hf + c];
@@ -437,15 +451,15 @@ __global__ void __launch_bounds__(kSsdThreads, 4) ssd_fwd_kernel(SsdArgs a, cons
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const int p = c * 8 + 2 * e;
-            const float2 xf = unpack_bf16(xin[e]);
+            const float2 xf = unpack2<F16>(xin[e]);
             float y0 = fmaf(eo, yo[p], yd[p]) + sD[16 * hf + p] * xf.x;
             float y1 = fmaf(eo, yo[p + 1], yd[p + 1]) + sD[16 * hf + p + 1] * xf.y;
             if (zbase != nullptr) {
-              const float2 zf = unpack_bf16(zin[e]);
+              const float2 zf = unpack2<F16>(zin[e]);
               y0 *= silu_f(zf.x);
               y1 *= silu_f(zf.y);
             }
-            o[e] = pack_bf16(y0, y1);
+            o[e] = pack2<F16>(y0, y1);
           }
           *reinterpret_cast<uint4*>(orow + c * 8) = make_uint4(o[0], o[1], o[2], o[3]);
         }
@@ -490,17 +504,17 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// Tensor map of a bf16 tensor seen as (8 elements, seqlen, pieces of 8 columns, group or head,
+// Tensor map of a bf16 / fp16 tensor seen as (8 elements, seqlen, pieces of 8 columns, group or head,
 // batch) with element strides (1, s_l, 8, s_g, s_b); box (8, 128, box_pieces, 1, 1).
 bool encode_map(CUtensorMap* m, const void* base, int64_t L, int64_t pieces, int64_t ng, int64_t nb, int64_t s_l,
-                int64_t s_g, int64_t s_b, int box_pieces) {
+                int64_t s_g, int64_t s_b, int box_pieces, bool f16) {
   PFN_cuTensorMapEncodeTiled_v12000 fn = encode_fn();
   if (fn == nullptr) return false;
   const cuuint64_t dims[5] = {8, (cuuint64_t)L, (cuuint64_t)pieces, (cuuint64_t)ng, (cuuint64_t)nb};
   const cuuint64_t strides[4] = {(cuuint64_t)s_l * 2, 16, (cuuint64_t)s_g * 2, (cuuint64_t)s_b * 2};
   const cuuint32_t box[5] = {8, (cuuint32_t)kQ, (cuuint32_t)box_pieces, 1, 1};
   const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
-  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, const_cast<void*>(base), dims, strides, box, estr,
+  return fn(m, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, const_cast<void*>(base), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -523,8 +537,9 @@ MB200_API int mb200_ssd_chunk_scan_fwd(const mb200_ssd_params* p, void* stream) 
   if (p->batch < 0 || p->seqlen < 0 || p->nheads < 0 || p->headdim <= 0 || p->ngroups <= 0 || p->dstate <= 0)
     return MB200_ERR_BAD_SHAPE;
   if (p->nheads % p->ngroups != 0) return MB200_ERR_BAD_SHAPE;
-  if (p->x_dtype != MB200_BF16) return p->x_dtype == MB200_F32 || p->x_dtype == MB200_F16 ? MB200_ERR_UNSUPPORTED
-                                                                                          : MB200_ERR_BAD_DTYPE;
+  if (p->x_dtype != MB200_BF16 && p->x_dtype != MB200_F16)
+    return p->x_dtype == MB200_F32 ? MB200_ERR_UNSUPPORTED : MB200_ERR_BAD_DTYPE;
+  const bool f16 = p->x_dtype == MB200_F16;
   if (p->dstate % 8 != 0 || p->dstate > kNP || p->headdim % kPT != 0 || p->headdim > 256 || p->seqlen > 0x7fffffff)
     return MB200_ERR_UNSUPPORTED;
   // 16-byte pieces: row starts of x, z, B, C and out aligned
@@ -542,16 +557,16 @@ MB200_API int mb200_ssd_chunk_scan_fwd(const mb200_ssd_params* p, void* stream) 
   if (ctas == 0) return MB200_OK;
   if (ctas > 0x7fffffff) return MB200_ERR_UNSUPPORTED;
   SsdArgs a;
-  a.x = static_cast<const __nv_bfloat16*>(p->x);
+  a.x = static_cast<const uint16_t*>(p->x);
   a.dt = p->dt;
   a.A = p->A;
-  a.B = static_cast<const __nv_bfloat16*>(p->B);
-  a.C = static_cast<const __nv_bfloat16*>(p->C);
+  a.B = static_cast<const uint16_t*>(p->B);
+  a.C = static_cast<const uint16_t*>(p->C);
   a.D = p->D;
-  a.z = static_cast<const __nv_bfloat16*>(p->z);
+  a.z = static_cast<const uint16_t*>(p->z);
   a.dt_bias = p->dt_bias;
   a.init = p->initial_states;
-  a.out = static_cast<__nv_bfloat16*>(p->out);
+  a.out = static_cast<uint16_t*>(p->out);
   a.final_states = p->final_states;
   a.L = p->seqlen, a.H = p->nheads, a.P = p->headdim, a.G = p->ngroups, a.N = p->dstate;
   a.xbs = p->x_batch_stride, a.xls = p->x_seqlen_stride, a.xhs = p->x_head_stride;
@@ -567,13 +582,15 @@ MB200_API int mb200_ssd_chunk_scan_fwd(const mb200_ssd_params* p, void* stream) 
   SsdMaps maps;
   const int64_t L = p->seqlen > 0 ? p->seqlen : 1;
   if (!encode_map(&maps.B, p->B, L, p->dstate / 8, p->ngroups, p->batch, p->B_seqlen_stride, p->B_group_stride,
-                  p->B_batch_stride, (int)(p->dstate / 8)) ||
+                  p->B_batch_stride, (int)(p->dstate / 8), f16) ||
       !encode_map(&maps.C, p->C, L, p->dstate / 8, p->ngroups, p->batch, p->C_seqlen_stride, p->C_group_stride,
-                  p->C_batch_stride, (int)(p->dstate / 8)) ||
+                  p->C_batch_stride, (int)(p->dstate / 8), f16) ||
       !encode_map(&maps.x, p->x, L, p->headdim / 8, p->nheads, p->batch, p->x_seqlen_stride, p->x_head_stride,
-                  p->x_batch_stride, kPT / 8))
+                  p->x_batch_stride, kPT / 8, f16))
     return MB200_ERR_CUDA;
-  const auto kern = p->seq_idx != nullptr ? ssd_fwd_kernel<true> : ssd_fwd_kernel<false>;
+  const bool seq = p->seq_idx != nullptr;
+  const auto kern = f16 ? (seq ? ssd_fwd_kernel<true, true> : ssd_fwd_kernel<false, true>)
+                        : (seq ? ssd_fwd_kernel<true, false> : ssd_fwd_kernel<false, false>);
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSsdSmem);
   if (e != cudaSuccess) return MB200_ERR_CUDA;
   kern<<<(unsigned)ctas, kSsdThreads, kSsdSmem, static_cast<cudaStream_t>(stream)>>>(a, maps);

@@ -112,12 +112,13 @@ def ssd_chunk_scan(x, dt, A, B, C, chunk_size, D=None, z=None, dt_bias=None, ini
                    cu_seqlens=None, dt_softplus=False, dt_limit=(0.0, float("inf")), return_final_states=False,
                    return_varlen_states=False):
     """``mamba_chunk_scan_combined`` for transformers' Mamba-2 mixer. The SSD kernel multiplies in
-    bf16: x, z, B and C of another dtype (an fp32 model) are rounded to bf16 and the output is
-    returned in x's dtype (upstream's Triton kernels likewise multiply fp32 inputs in tf32)."""
+    bf16 or fp16: x, z, B and C of an fp32 model are rounded to bf16 and the output is returned in
+    x's dtype (upstream's Triton kernels likewise multiply fp32 inputs in tf32)."""
     dtype = x.dtype
+    work = dtype if dtype in (torch.bfloat16, torch.float16) else torch.bfloat16
 
     def bf(t):
-        return None if t is None else (t if t.dtype == torch.bfloat16 else t.to(torch.bfloat16))
+        return None if t is None else (t if t.dtype == work else t.to(work))
 
     r = mamba_chunk_scan_combined(bf(x), dt, A, bf(B), bf(C), chunk_size, D=D, z=bf(z), dt_bias=dt_bias,
                                   initial_states=initial_states, seq_idx=seq_idx, cu_seqlens=cu_seqlens,

@@ -129,7 +129,8 @@ def mamba_chunk_scan_combined(
     dt is clamped to ``dt_limit`` after the bias and the optional softplus (threshold 20), as
     upstream does; the default (0, inf) only removes negative steps. ``chunk_size`` is checked
     and otherwise does not change the result beyond rounding: the kernel always works in chunks
-    of 64 steps. This build takes bf16 x / z (B and C are used in bf16), dstate a multiple of 8
+    of 64 steps. This build takes bf16 or fp16 x / z (B and C are used in x's dtype; the products
+    run in that 16-bit type with float32 accumulation), dstate a multiple of 8
     up to 128 and headdim a multiple of 32 up to 256.
 
     ``seq_idx`` (batch, seqlen), non-decreasing along seqlen, packs several sequences into one
@@ -165,8 +166,9 @@ def mamba_chunk_scan_combined(
         raise ValueError(f"initial_states must be {(b, h, p, n)}, got {tuple(initial_states.shape)}")
     if seq_idx is not None and tuple(seq_idx.shape) != (b, l):
         raise ValueError(f"seq_idx must be {(b, l)}, got {tuple(seq_idx.shape)}")
-    if x.dtype != torch.bfloat16:
-        raise NotImplementedError(f"mamba_chunk_scan_combined: x dtype {x.dtype} (this build takes bfloat16)")
+    if x.dtype not in (torch.bfloat16, torch.float16):
+        raise NotImplementedError(f"mamba_chunk_scan_combined: x dtype {x.dtype} (this build takes bfloat16 or "
+                                  "float16)")
     if n % 8 != 0 or n > 128 or p % 32 != 0 or p > 256:
         raise NotImplementedError(f"mamba_chunk_scan_combined: dstate {n} / headdim {p} outside this build "
                                   "(dstate a multiple of 8 up to 128, headdim a multiple of 32 up to 256)")

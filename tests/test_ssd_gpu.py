@@ -211,3 +211,24 @@ def test_ssd_long_sequence_slice():
     out, fin, ro, rf = _run_both(inp)
     _close(out, ro, 1e-2, "out")
     _close(fin, rf, 5e-3, "final_states")
+
+
+@pytest.mark.parametrize("b,l,h,p,g,n,init,seq", [
+    (2, 333, 2, 64, 1, 64, True, False),
+    (1, 700, 2, 128, 2, 128, False, False),
+    (2, 300, 4, 32, 1, 24, False, True),
+])
+def test_ssd_fp16_inputs(b, l, h, p, g, n, init, seq):
+    """fp16 x / z / B / C: the products run on fp16 operands (kind::f16 with the fp16 format)."""
+    inp = _inputs(b, l, h, p, g, n, seed=41, regime="wide", init=init)
+    for k in ("x", "z", "B", "C"):
+        inp[k] = inp[k].float().to(torch.float16)
+    seq_idx = None
+    if seq:
+        seq_idx = torch.zeros(b, l, dtype=torch.int32)
+        seq_idx[:, 90:] = 1
+        seq_idx[:, 200:] = 2
+    out, fin, ro, rf = _run_both(inp, seq_idx=seq_idx)
+    assert out.dtype == torch.float16
+    _close(out, ro, 1e-2, "out")
+    _close(fin, rf, 5e-3, "final_states")
