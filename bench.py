@@ -23,7 +23,8 @@ ranks); each phase is replayed from a CUDA graph, so host launch latency is not 
 host memory and every output and gradient copied back, all inside the timed region; consecutive
 steps are pipelined (copies of neighbouring steps overlap the current step's kernels).
 
-At N = 1 the line also carries a "c2" block: BASELINE config 2 (fp32, batch 4, dim 1536, seqlen
+At N = 1 the line also carries a "c1" block (the reference README's forward-only
+fp32 shape, with its roofline and the reference kernel's CPU time on the same problem), a "c2" block: BASELINE config 2 (fp32, batch 4, dim 1536, seqlen
 1024, z, delta_bias), the north-star's fp32 configuration, with its own roofline and CPU baseline;
 and "c3" / "c4" blocks: BASELINE configs 3 and 4 at model level (transformers' MambaForCausalLM,
 random init, routed to this package by hf.patch_transformers): the 130M prefill in fp32 and the
@@ -691,6 +692,105 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+C1 = dict(batch=1, dim=1536, seqlen=2048, dstate=16,
+          desc="BASELINE config 1: selective_scan_fn forward only, fp32, b=1 d=1536 l=2048 n=16, softplus, no z / "
+               "delta_bias (the reference README's direct-use shape)")
+
+
+def c1_inputs(torch, dev):
+    b, d, l, n = (C1[k] for k in ("batch", "dim", "seqlen", "dstate"))
+    g = torch.Generator(device=dev).manual_seed(11)
+    r = lambda *s: torch.randn(*s, generator=g, device=dev)  # noqa: E731
+    return dict(u=r(b, d, l), delta=r(b, d, l), A=-torch.rand(d, n, generator=g, device=dev), B=r(b, 1, n, l),
+                C=r(b, 1, n, l), D=r(d))
+
+
+def c1_timing(args, ctx, peak, peak_kind):
+    """Device-timed forward of BASELINE config 1 (inputs under L2: a 256 MiB write before each step)."""
+    torch, dev = ctx["torch"], ctx["dev"]
+    from mamba_cpu_b200 import _lib
+
+    b, d, l, n = (C1[k] for k in ("batch", "dim", "seqlen", "dstate"))
+    x = c1_inputs(torch, dev)
+    ops = torch.ops.mamba_b200
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+
+    def fwd():
+        return ops.selective_scan_fwd(x["u"], x["delta"], x["A"], x["B"], x["C"], x["D"], None, None, True)
+    stream = torch.cuda.Stream(device=dev)
+    stream.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            fwd()
+    torch.cuda.current_stream(dev).wait_stream(stream)
+    launches = _lib.last_launch_count()
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        fwd()
+    steps = max(args.steps, 20)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for _ in range(max(3, args.warmup)):
+        flush.zero_()
+        graph.replay()
+    torch.cuda.synchronize(dev)
+    with Clocks(ctx["local"]) as clk:
+        for e0, e1 in evs:
+            flush.zero_()
+            e0.record()
+            graph.replay()
+            e1.record()
+        torch.cuda.synchronize(dev)
+    ms = sum(e0.elapsed_time(e1) for e0, e1 in evs) / steps
+    del graph
+    E = b * d * l
+    fwd_bytes, _ = algorithmic_bytes(b, d, l, n, 4, 4, False)
+    return {"workload": C1["desc"], "value": E / (ms * 1e-3), "unit": "elements/s", "ms_per_step": ms,
+            "steps": steps, "l2": "flushed (256 MiB write) before every step",
+            "roofline_fwd": roofline_block("forward", "scan_fwd_kernel", fwd_bytes, ms, peak, peak_kind, None, E),
+            "gpu_launches": launches * steps, "clocks": clk.summary()}
+
+
+def c1_cpu_baseline(budget_s):
+    """The reference's forward kernel (oracle/_ref) on the whole config-1 problem, all host threads."""
+    import torch
+
+    import oracle
+    from oracle import f64, ref_c
+
+    cores = _host_cores()
+    torch.set_num_threads(cores)
+    b, d, l, n = (C1[k] for k in ("batch", "dim", "seqlen", "dstate"))
+    x = c1_inputs(torch, torch.device("cpu"))
+    Bk = x["B"].transpose(-1, -2).contiguous()  # (b, g, l, n): selective_scan_interface.py:131-135
+    Ck = x["C"].transpose(-1, -2).contiguous()
+    out, last = torch.empty(b, d, l), torch.empty(b, d, n)
+    P = lambda t: t.data_ptr()  # noqa: E731
+    if oracle.ref_available():
+        kind = "reference"
+
+        def step():
+            ref_c.selective_scan_fwd_f32(P(x["u"]), P(x["delta"]), P(x["A"]), P(Bk), P(Ck), P(x["D"]), 0, 0, P(out),
+                                         P(last), b, d, l, n, 1, True, cores)
+    else:
+        kind = "port"
+        f64.set_num_threads(cores)
+
+        def step():
+            f64.scan_fwd(x["u"], x["delta"], x["A"], x["B"], x["C"], x["D"], delta_softplus=True)
+    t0 = time.perf_counter()
+    step()
+    first = time.perf_counter() - t0
+    iters = max(1, min(20, int(budget_s / max(first, 1e-3))))
+    t0 = time.perf_counter()
+    for _ in range(iters):
+        step()
+    dt = (time.perf_counter() - t0) / iters
+    return {"value": b * d * l / dt, "unit": "elements/s", "cores": cores, "kind": kind,
+            "sample": f"{iters} timed forward passes (after 1 warm-up) of the whole config-1 problem, {cores} threads, "
+                      f"time.perf_counter", "ms_per_step": dt * 1e3}
+
+
 SSD = dict(batch=2, seqlen=4096, nheads=80, headdim=64, ngroups=1, dstate=128,
            desc="Mamba-2 SSD chunk scan forward (mamba_chunk_scan_combined, a roadmap item of the reference) at the "
                 "Mamba-2 2.7B layer shape: b=2, seqlen 4096, 80 heads x headdim 64 (d_inner 5120), dstate 128, "
@@ -844,9 +944,11 @@ def run_ours(args):
         for name in ("c3", "c4"):
             models[name] = model_timing(name, args, ctx)
     peak, peak_kind = load_peak()
-    ssd = None
+    ssd = c1 = None
     if world == 1 and not args.no_ssd:
         ssd = ssd_timing(args, ctx, peak, peak_kind)
+    if world == 1 and not args.no_c2:
+        c1 = c1_timing(args, ctx, peak, peak_kind)
     if group is not None:
         dist.barrier()
         dist.destroy_process_group()
@@ -924,6 +1026,10 @@ def run_ours(args):
         if not args.no_cpu_baseline:
             line["c2"]["cpu_baseline"] = cpu_baseline(CONFIGS["c2"], args.cpu_budget)
     line.update(models)
+    if c1 is not None:
+        if not args.no_cpu_baseline:
+            c1["cpu_baseline"] = c1_cpu_baseline(args.cpu_budget)
+        line["c1"] = c1
     if ssd is not None:
         if not args.no_cpu_baseline:
             ssd["cpu_baseline"] = ssd_cpu_baseline(args.cpu_budget)
@@ -940,7 +1046,7 @@ def main():
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true", help="device timing only (for profiler runs)")
-    p.add_argument("--no-c2", action="store_true", help="skip the config-2 block of the N=1 line")
+    p.add_argument("--no-c2", action="store_true", help="skip the config-1 and config-2 blocks of the N=1 line")
     p.add_argument("--no-models", action="store_true",
                    help="skip the model-level config-3 / config-4 blocks of the N=1 line")
     p.add_argument("--no-ssd", action="store_true", help="skip the Mamba-2 SSD block of the N=1 line")
