@@ -113,7 +113,12 @@ FwdLayout fwd_layout(const ScanArgs& a) {
   FwdLayout w = {};
   w.pieces = 1;
   w.piece_chunks = a.nchunks;
-  if (a.batch > 0 && a.dim > 0) piece_split(fwd_ctas(a), a.nchunks, false, &w.pieces, &w.piece_chunks);
+  // Short rows of small problems (the one-state-per-lane layout) stay whole unless a count is
+  // forced: there the summary pass's own chain is as long as the pieces it would save (BASELINE
+  // config 1, b=1 d=1536 l=2048: 71.7 us whole, 93.2 us in the 2 pieces the cost model picks).
+  const bool short_rows = fwd_states_per_lane(a.batch * a.dim, a.nchunks) == 1;
+  if (a.batch > 0 && a.dim > 0 && (!short_rows || forced_pieces() > 0))
+    piece_split(fwd_ctas(a), a.nchunks, false, &w.pieces, &w.piece_chunks);
   const size_t per = sizeof(float) * (size_t)(w.pieces - 1) * a.batch * a.dim * a.N;
   ScanArgs t = a;
   t.pieces = w.pieces;

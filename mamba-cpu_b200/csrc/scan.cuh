@@ -82,6 +82,7 @@ struct BwdArgs {
 // forces a count (tests).
 int seq_pieces(int64_t ctas, int nchunks, bool backward);
 void set_forced_pieces(int n);  // 0: automatic
+int forced_pieces();             // the count set by set_forced_pieces (0: automatic)
 int sm_count();
 // CTAs of the forward over whole rows (its per-CTA channel count depends on the lane layout).
 int64_t fwd_ctas(const ScanArgs& a);

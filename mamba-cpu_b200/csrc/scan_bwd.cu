@@ -876,6 +876,7 @@ int sm_count() {
 std::atomic<int> g_forced_pieces{0};
 
 void set_forced_pieces(int n) { g_forced_pieces.store(n > 0 ? n : 0); }
+int forced_pieces() { return g_forced_pieces.load(); }
 
 int seq_pieces(int64_t ctas, int nchunks, bool backward) {
   // Pieces trade a summary pass over all pieces but one (relative cost s per element: measured
