@@ -492,15 +492,16 @@ __global__ void __launch_bounds__(kSsdThreads, 4) ssd_fwd_kernel(SsdArgs a, cons
 }
 
 // cuTensorMapEncodeTiled from the driver (through the runtime, no libcuda link).
+// Looked up once per process (a function-local static: thread-safe initialisation).
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (fn == nullptr) {
+  static const PFN_cuTensorMapEncodeTiled_v12000 fn = []() -> PFN_cuTensorMapEncodeTiled_v12000 {
     void* p = nullptr;
     cudaDriverEntryPointQueryResult q;
     if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
         q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  }
+      return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    return nullptr;
+  }();
   return fn;
 }
 

@@ -41,6 +41,33 @@ def test_automatic_piece_count():
     assert pieces(640, 1024, 0) == 1
 
 
+def _fwd_params(batch, dim, seqlen, dstate=16):
+    p = _lib.ScanFwdParams()
+    p.u = p.delta = p.A = p.B = p.C = p.out = 0x1000
+    p.batch, p.dim, p.seqlen, p.dstate, p.ngroups = batch, dim, seqlen, dstate, 1
+    p.B_batch_stride = p.C_batch_stride = dstate * seqlen
+    p.B_group_stride = p.C_group_stride = dstate * seqlen
+    p.B_dstate_stride = p.C_dstate_stride = seqlen
+    p.B_seqlen_stride = p.C_seqlen_stride = 1
+    return p
+
+
+def test_forward_keeps_short_rows_whole():
+    """Short rows of small problems (under 64 chunks and 4096 rows) are not split by the automatic
+    choice: the forward's piece summaries would need workspace, and there is none (BASELINE
+    config 1's shape); a forced count still splits them, and long rows of few channels still split."""
+    if torch.cuda.is_available():
+        pytest.skip("the long-row case's slot count comes from the GPU here")
+    ws = _lib.lib.mb200_selective_scan_fwd_workspace_size
+    assert ws(_fwd_params(1, 1536, 2048)) == 0           # config 1: whole rows
+    _lib.set_sequence_pieces(2)
+    try:
+        assert ws(_fwd_params(1, 1536, 2048)) > 0        # forced: split
+    finally:
+        _lib.set_sequence_pieces(0)
+    assert ws(_fwd_params(2, 640, 65536)) > 0            # one rank's config-5 shard at 8 ranks
+
+
 # ---------------------------------------------------------------------------------------------
 # GPU parity
 
