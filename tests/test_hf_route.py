@@ -97,6 +97,27 @@ def test_patch_covers_other_families(family):
     assert {n: getattr(mod, n, "<missing>") for n in names} == before
 
 
+def test_patch_covers_mamba2():
+    """Mamba-2 resolves mamba_chunk_scan_combined / mamba_split_conv1d_scan_combined through
+    "mamba-ssm"; a mixer built while patched reads the fast-path flag in forward, so unpatching
+    leaves that flag False (transformers' own sequential path) rather than deleting it."""
+    from transformers import Mamba2Config, Mamba2Model
+    from transformers.models.mamba2 import modeling_mamba2 as m2
+
+    names = ("causal_conv1d_fn", "causal_conv1d_update", "selective_state_update", "mamba_chunk_scan_combined",
+             "mamba_split_conv1d_scan_combined")
+    with _patched():
+        Mamba2Model(Mamba2Config(vocab_size=32, hidden_size=64, state_size=16, num_heads=2, head_dim=64, expand=2,
+                                 n_groups=1, num_hidden_layers=1))
+        assert m2.is_fast_path_available is True
+        assert m2.mamba_chunk_scan_combined is hf.ssd_chunk_scan
+        assert m2.mamba_split_conv1d_scan_combined is hf.mamba_split_conv1d_scan_combined
+        for n in names:
+            assert getattr(m2, n) is not None, n
+    assert m2.is_fast_path_available is False
+    assert all(getattr(m2, n, None) is not hf.ssd_chunk_scan for n in names)
+
+
 def test_mamba_inner_fn_signature_matches_mamba_ssm():
     import inspect
 
